@@ -1,0 +1,381 @@
+"""Benchmark of the paged decode attention hot path (config 2) on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload: GQA paged decode, bf16, 64 sequences with
+k_len ~ U[1024, 8192], 32 q heads / 8 kv heads, head_dim 128, block 16, pool of
+ceil(1.25 * sum(k_len) / 16) blocks with shuffled block tables, q/k/v ~ N(0, 1).
+Synthetic seeded data (no dataset exists for it). One step = one
+paged_flash_attention call over the whole batch (one layer of one decode step).
+
+With N GPUs (torchrun, one process per GPU) the (sequence, kv head) units are
+sharded by kv head: each rank owns 8/N kv heads (32/N q heads) of a global
+batch of 64*N sequences, so per-GPU work stays at the config-2 size (weak
+scaling) and no data crosses GPUs. ``value`` is the aggregate KV bytes read
+per second over all ranks, timed as the max over ranks.
+
+``e2e`` is the same metric through the public API with host buffers: each step
+copies that step's q and packed metadata (block tables, lengths) from pinned
+host memory, runs the attention and reads O and LSE back to pinned host
+memory, timed by wall clock. The KV pool is device-resident engine state (it
+is never a per-step input in the serving engine), so it is not copied.
+
+``--impl reference`` times the reference algorithm on the host cores instead
+(the numpy restatement in oracle/, the reference being Python/torch code that
+is not installed on the GPU box) on a bounded sample of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import re
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+import torch
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO))
+
+METRIC = "paged-decode KV-read GB/s (% of HBM peak); end-to-end decode tokens/sec"
+FALLBACK_HBM_GBS = 6650.0
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--batch", type=int, default=64)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def peaks():
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return FALLBACK_HBM_GBS, "fallback"
+
+
+def profiled_traffic():
+    """dram bytes per launch of the decode kernel from the committed ncu summary
+    (a line 'traffic_bytes_per_launch: N'), or None."""
+    p = REPO / "profiles" / "paged_decode_config2.md"
+    if not p.exists():
+        return None
+    m = re.search(r"traffic_bytes_per_launch:\s*([0-9.eE+]+)", p.read_text())
+    return float(m.group(1)) if m else None
+
+
+class ClockSampler:
+    """nvidia-smi clock/throttle samples every 100 ms while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.idx = gpu_index
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.idx), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"], "samples": 0}
+        self.proc.terminate()
+        out, _ = self.proc.communicate(timeout=10)
+        rows = [[c.strip() for c in line.split(",")] for line in out.strip().splitlines() if line.strip()]
+        sm = [float(r[1]) for r in rows if len(r) >= 9 and r[1].replace(".", "").isdigit()]
+        smax = [float(r[2]) for r in rows if len(r) >= 9 and r[2].replace(".", "").isdigit()]
+        reasons = set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            if len(r) < 9:
+                continue
+            for name, val in zip(names, r[5:9]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(smax) if smax else None,
+                "reasons": sorted(reasons), "samples": len(rows)}
+
+
+# --------------------------------------------------------------- our arm
+def shard_batch(args, rank: int, world: int, device):
+    from serving_engine_b200 import workloads
+
+    if 8 % world or 32 % world:
+        raise SystemExit(f"--gpus {world} must divide the 8 kv heads")
+    b = workloads.decode_batch(args.batch * world, 1024, 8192, 32 // world, 8 // world, 128, torch.bfloat16,
+                               seed=args.seed * 1000 + rank, fill=str(device))
+    return b
+
+
+def run_ours(args, rank, world, device, dist):
+    from serving_engine_b200 import ops, paged_flash_attention
+    from serving_engine_b200.paged_attention import metadata_from_lists
+
+    b = shard_batch(args, rank, world, device)
+    hq, hkv = b.num_q_heads, b.num_kv_heads
+    md = metadata_from_lists(b.q_lens, b.k_lens, b.q_starts, b.q_pos_offsets, b.block_tables, device)
+    q = b.q.to(device)
+    kv_bytes_rank = b.kv_bytes()
+    stream = torch.cuda.current_stream(device)
+
+    def step():
+        return paged_flash_attention(q, b.k_cache, b.v_cache, md, hq, hkv, b.scale)
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize(device)
+    ops.check_device_errors(device)
+
+    sampler = ClockSampler(device.index if device.index is not None else 0)
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize(device)
+    sampler.start()
+    time.sleep(0.3)  # let nvidia-smi start sampling before the timed region
+    launches0 = ops.LAUNCHES[0]
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    for _ in range(args.steps):
+        step()
+    ev1.record(stream)
+    torch.cuda.synchronize(device)
+    launches = ops.LAUNCHES[0] - launches0
+    clocks = sampler.stop()
+    ms_total = ev0.elapsed_time(ev1)
+    t = torch.tensor([ms_total], dtype=torch.float64, device=device)
+    if dist is not None:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dist.barrier()
+    ms_total_max = float(t.item())
+    ms_per_step = ms_total_max / args.steps
+    agg_bytes = kv_bytes_rank * world
+    value = agg_bytes / (ms_per_step * 1e-3) / 1e9
+    per_rank_gbs = kv_bytes_rank / (ms_total / args.steps * 1e-3) / 1e9
+    ops.check_device_errors(device)
+
+    # ---- e2e through the public API with host buffers
+    e2e = run_e2e(args, b, device, dist, world)
+
+    result = {
+        "metric": METRIC,
+        "value": round(value, 2),
+        "unit": "GB/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms_per_step, 5),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic (seeded N(0,1) q/k/v; k_len ~ U[1024,8192]; shuffled block tables)",
+        "config": {
+            "workload": "config 2: GQA paged decode, batch 64/GPU, k_len U[1024,8192], 32q/8kv heads, head_dim 128, "
+                        "block 16, pool 1.25x tokens",
+            "global_batch": args.batch * world,
+            "seq_len": "U[1024,8192]",
+            "parallelism": f"kv-head shard x{world} (no communication)",
+            "kv_bytes_per_step_per_gpu": kv_bytes_rank,
+            "l2": "inputs larger than L2 (KV ~1.2 GB per step per GPU vs 126 MB L2); no flush",
+        },
+        "gpu_launches": launches,
+        "clocks": clocks,
+        "e2e": e2e,
+    }
+    hbm, src = peaks()
+    traffic = profiled_traffic()
+    result["roofline"] = {
+        "bound": "hbm",
+        "achieved": round(per_rank_gbs, 2),
+        "peak": hbm,
+        "unit": "GB/s",
+        "frac": round(per_rank_gbs / hbm, 4),
+        "peak_source": f"{src} (MEASURED_PEAKS.json hbm_gbs)" if src == "measured" else "fallback 6.65 TB/s",
+        "frac_of_nominal_8000": round(per_rank_gbs / 8000.0, 4),
+        "kernel": "decode_mma_kernel + decode_combine_kernel (one paged_flash_attention call)",
+        "traffic": traffic,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        result["cpu_baseline"] = cpu_baseline(b, budget_s=12.0)
+    return result
+
+
+def run_e2e(args, b, device, dist, world):
+    from serving_engine_b200 import paged_flash_attention
+    from serving_engine_b200.paged_attention import metadata_from_lists
+
+    q_host = b.q.pin_memory()
+    o_host = torch.empty_like(q_host).pin_memory()
+    lse_host = torch.empty(q_host.shape[0], b.num_q_heads, dtype=torch.float32).pin_memory()
+    rows = len(b.q_lens)
+    width = max(len(t) for t in b.block_tables)
+    meta_bytes = 4 * (4 * rows + rows * width + sum(b.q_lens))
+    h2d = q_host.numel() * q_host.element_size() + meta_bytes
+    d2h = o_host.numel() * o_host.element_size() + lse_host.numel() * 4
+
+    def step():
+        md = metadata_from_lists(b.q_lens, b.k_lens, b.q_starts, b.q_pos_offsets, b.block_tables, device)
+        q = q_host.to(device, non_blocking=True)
+        o, lse = paged_flash_attention(q, b.k_cache, b.v_cache, md, b.num_q_heads, b.num_kv_heads, b.scale)
+        o_host.copy_(o, non_blocking=True)
+        lse_host.copy_(lse, non_blocking=True)
+        torch.cuda.current_stream(device).synchronize()
+
+    n = max(10, min(args.steps // 10, 200))
+    for _ in range(3):
+        step()
+    if dist is not None:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for _ in range(n):
+        step()
+    dt = time.perf_counter() - t0
+    t = torch.tensor([dt], dtype=torch.float64, device=device)
+    if dist is not None:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    dt = float(t.item())
+    gbs = b.kv_bytes() * world * n / dt / 1e9
+    return {"value": round(gbs, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+            "steps": n, "ms_per_step": round(dt / n * 1e3, 4),
+            "how": "wall clock; per step: packed metadata + q H2D from pinned host, attention, O+LSE D2H, sync"}
+
+
+# ------------------------------------------------------ CPU baseline / reference arm
+def _host_sample(b, rows):
+    """Host copies of the sampled rows' KV blocks, re-indexed into a compact pool."""
+    tables, blocks = [], []
+    for r in rows:
+        n = math.ceil(b.k_lens[r] / 16)
+        ids = list(b.block_tables[r][:n])
+        tables.append(list(range(len(blocks), len(blocks) + n)))
+        blocks.extend(ids)
+    idx = torch.tensor(blocks, dtype=torch.long, device=b.k_cache.device)
+    kc = b.k_cache.index_select(0, idx).float().cpu().numpy()
+    vc = b.v_cache.index_select(0, idx).float().cpu().numpy()
+    q = b.q[rows].float().cpu().numpy()
+    return q, kc, vc, tables
+
+
+def cpu_sample_run(b, rows, q, kc, vc, tables):
+    import numpy as np
+
+    from oracle.paged_attention import paged_attention
+
+    width = max(len(t) for t in tables)
+    bt = np.array([t + [0] * (width - len(t)) for t in tables])
+    k_lens = [b.k_lens[r] for r in rows]
+    t0 = time.perf_counter()
+    paged_attention(q, kc, vc, bt, list(range(len(rows))), [1] * len(rows), k_lens, [k - 1 for k in k_lens],
+                    b.scale, True, dtype=np.float32)
+    dt = time.perf_counter() - t0
+    nbytes = sum(k_lens) * b.num_kv_heads * b.head_dim * 2 * 2  # bf16-equivalent KV bytes
+    return nbytes, dt
+
+
+def cpu_baseline(b, budget_s: float) -> dict:
+    """The oracle (numpy, float32) on sampled config-2 rows, ~budget_s of CPU work."""
+    cores = os.cpu_count() or 1
+    rows_all = list(range(len(b.k_lens)))
+    done_bytes, done_t, used = 0, 0.0, []
+    i = 0
+    while done_t < budget_s and i < len(rows_all):
+        rows = rows_all[i:i + 4]
+        i += 4
+        q, kc, vc, tables = _host_sample(b, rows)
+        nb, dt = cpu_sample_run(b, rows, q, kc, vc, tables)
+        done_bytes += nb
+        done_t += dt
+        used += rows
+    gbs = done_bytes / done_t / 1e9
+    return {"value": round(gbs, 4), "unit": "GB/s", "cores": cores, "kind": "port",
+            "sample": f"{len(used)} of {len(rows_all)} config-2 sequences ({done_bytes / 1e9:.2f} GB bf16-equivalent KV, "
+                      f"{done_t:.1f} s), oracle/paged_attention.py in numpy float32 (multithreaded BLAS)"}
+
+
+def run_reference(args, device):
+    from serving_engine_b200 import workloads
+
+    b = workloads.config2(seed=args.seed, batch=args.batch, fill=str(device) if device else "cpu")
+    cores = os.cpu_count() or 1
+    rows_per_step = 2
+    samples = []
+    total_bytes, total_t = 0, 0.0
+    for s in range(args.warmup + args.steps):
+        rows = [(s * rows_per_step + j) % len(b.k_lens) for j in range(rows_per_step)]
+        q, kc, vc, tables = _host_sample(b, rows)
+        nb, dt = cpu_sample_run(b, rows, q, kc, vc, tables)
+        if s >= args.warmup:
+            total_bytes += nb
+            total_t += dt
+            samples.append(dt)
+        if total_t > 150:  # keep the whole arm within a few minutes
+            break
+    gbs = total_bytes / total_t / 1e9
+    n_steps = len(samples)
+    return {
+        "metric": METRIC, "value": round(gbs, 4), "unit": "GB/s", "n_gpus": args.gpus, "steps": n_steps,
+        "warmup": args.warmup, "ms_per_step": round(total_t / max(n_steps, 1) * 1e3, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32 (bf16-valued inputs)", "data": "synthetic",
+        "impl": "reference",
+        "config": {"workload": "config 2: GQA paged decode, batch 64, k_len U[1024,8192], 32q/8kv heads, head_dim 128",
+                   "global_batch": args.batch, "seq_len": "U[1024,8192]", "parallelism": "host cores"},
+        "cpu_baseline": {"value": round(gbs, 4), "unit": "GB/s", "cores": cores, "kind": "port",
+                         "sample": f"{rows_per_step} sequences per step, oracle/paged_attention.py numpy float32"},
+        "e2e": {"value": round(gbs, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+def main():
+    args = parse_args()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        device = torch.device("cuda", local_rank) if torch.cuda.is_available() else None
+        if device is not None:
+            torch.cuda.set_device(device)
+        print(json.dumps(run_reference(args, device)), flush=True)
+        return
+
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as tdist
+
+        tdist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
+        dist = tdist
+    try:
+        result = run_ours(args, rank, world, device, dist)
+        if rank == 0:
+            print(json.dumps(result), flush=True)
+    finally:
+        if dist is not None:
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

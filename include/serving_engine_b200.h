@@ -1,0 +1,146 @@
+/*
+ * serving_engine_b200.h -- C ABI of the B200 (sm_100a) paged-KV attention backend.
+ *
+ * This library replaces the hot path of the serving engine's paged attention:
+ *   - the Triton paged FlashAttention kernel and its launcher
+ *       serving_engine/paged_attention_kernel.py:16-160
+ *   - the KV write of the duck-typed cache shim
+ *       serving_engine/model_runner.py:21-32 (_PagedKVCache.write, two index_copy_)
+ *   - a batched copy-on-write block copy for prefix-cache forks (the reference has
+ *     the hook point at serving_engine/block_manager.py:129-132 but no copy).
+ *
+ * Conventions shared by every entry point:
+ *   - All pointers are device pointers unless stated otherwise. No entry point
+ *     allocates or frees device memory; callers pass every buffer, including
+ *     workspaces whose size the *_workspace_size functions report.
+ *   - `stream` is a cudaStream_t (NULL = legacy default stream). Work is enqueued
+ *     asynchronously; no entry point synchronises the host.
+ *   - The KV pool of one layer is two contiguous arrays k_cache, v_cache, each
+ *     [num_blocks, SEB_BLOCK_SIZE, num_kv_heads, head_dim] (model_runner.py:101-110,
+ *     :42-45). Slot s of the flat view is block s / 16, row s % 16.
+ *   - Strides are in ELEMENTS; the innermost (head_dim) stride is always 1.
+ *   - Return value: SEB_OK, or an SEB_E* status when the host-side validation
+ *     rejects the arguments or a launch fails; seb_last_error() then holds a
+ *     message for the calling thread.
+ *   - `err` (optional, may be NULL) is a device int32 that kernels OR SEB_ERRBIT_*
+ *     flags into when they meet an out-of-range index at run time. The offending
+ *     access is skipped; kernels never trap. The caller zeroes it and reads it
+ *     back whenever it wants to check.
+ */
+#ifndef SERVING_ENGINE_B200_H
+#define SERVING_ENGINE_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define SEB_API __attribute__((visibility("default")))
+#else
+#define SEB_API
+#endif
+
+#define SEB_BLOCK_SIZE 16 /* tokens per KV block: serving_engine/block.py:7 */
+
+/* element types of q / k / v / out (the attention computes in fp32) */
+enum seb_dtype { SEB_F32 = 0, SEB_F16 = 1, SEB_BF16 = 2 };
+
+/* host-side status codes */
+enum seb_status {
+  SEB_OK = 0,
+  SEB_EINVAL = 1,       /* an argument is out of range, misaligned or NULL */
+  SEB_EUNSUPPORTED = 2, /* a valid shape this build has no kernel for */
+  SEB_ECUDA = 3,        /* a CUDA launch or attribute call failed */
+  SEB_EWORKSPACE = 4    /* the workspace passed is smaller than required */
+};
+
+/* device-side error bits ORed into *err */
+#define SEB_ERRBIT_BLOCK_ID 1u /* block_table entry outside [0, num_blocks) */
+#define SEB_ERRBIT_SLOT 2u     /* slot_mapping entry outside [0, num_blocks*16) */
+#define SEB_ERRBIT_TIMEOUT 4u  /* a bounded wait on an mbarrier gave up */
+#define SEB_ERRBIT_KLEN 8u     /* k_len larger than the block table row can hold */
+#define SEB_ERRBIT_META 16u    /* a row / query index outside the metadata arrays */
+
+SEB_API const char* seb_version(void);
+SEB_API const char* seb_status_string(int status);
+/* message of the last failing call on this host thread ("" if none) */
+SEB_API const char* seb_last_error(void);
+
+/*
+ * KV append: k_cache_flat[slot_mapping[t]] = k_new[t], same for V, for t < n_tokens.
+ * Replaces _PagedKVCache.write (serving_engine/model_runner.py:21-32), whose two
+ * index_copy_ calls scatter [n_tokens, num_kv_heads, head_dim] rows at int64
+ * write_index (slot semantics: ModelRunner._flat_slot, model_runner.py:127-129).
+ * k_new element (t, h, d) is at k_new + t*k_stride_token + h*k_stride_head + d.
+ * One launch writes both K and V. Duplicate slots race (as index_copy_ does on
+ * CUDA); out-of-range slots set SEB_ERRBIT_SLOT and are skipped.
+ */
+SEB_API int seb_kv_append(const void* k_new, int64_t k_stride_token, int64_t k_stride_head,
+                  const void* v_new, int64_t v_stride_token, int64_t v_stride_head,
+                  int64_t n_tokens, const int64_t* slot_mapping, void* k_cache, void* v_cache,
+                  int64_t num_blocks, int32_t num_kv_heads, int32_t head_dim, int32_t dtype,
+                  int32_t* err, void* stream);
+
+/*
+ * Batched block copy for copy-on-write: for every pair i < n_pairs and every
+ * layer l < num_layers and K/V plane p, block dst[i] := block src[i], i.e.
+ * kv_cache[:, :, dst] = kv_cache[:, :, src] on the engine's pool
+ * kv_cache[num_layers, 2, num_blocks, 16, num_kv_heads, head_dim]
+ * (model_runner.py:101-110). New: the reference's BlockManager.fork
+ * (block_manager.py:129-132) shares whole tables and never copies.
+ * `layer_stride_bytes` is the distance between layer l and l+1 in bytes (the
+ * full pool passes 2*num_blocks*block_bytes; a per-layer call passes any value
+ * with num_layers = 1). dst ids must be distinct and must not appear among src
+ * ids (validated by the caller; overlapping pairs race). Ids outside
+ * [0, num_blocks) set SEB_ERRBIT_BLOCK_ID and are skipped.
+ */
+SEB_API int seb_copy_blocks(void* kv_cache, int64_t num_layers, int64_t layer_stride_bytes,
+                    int64_t num_blocks, int64_t block_bytes, const int64_t* src,
+                    const int64_t* dst, int64_t n_pairs, int32_t* err, void* stream);
+
+/*
+ * Paged attention over the metadata of build_paged_batch_metadata
+ * (paged_attention_kernel.py:163-200), computed exactly as the reference kernel
+ * defines it (paged_attention_kernel.py:16-122): for row r, query i < q_lens[r]
+ * (token q_starts[r]+i, logical position q_pos_offsets[r]+i) and query head h,
+ *   O = softmax_j(scale * q.k_j [causal: k_j <= position]) . v_j,
+ *   LSE = m + log(l)   (natural log, fp32),
+ * over the keys j < k_lens[r] held at slots block_table[r, j/16]*16 + j%16 of
+ * kv head h / (num_q_heads/num_kv_heads). Keys in the last partial block beyond
+ * k_lens[r] are zero-padded exactly as the reference's boundary-checked loads
+ * make them (they matter only when is_causal = 0). A row with k_lens = 0 and
+ * q_lens > 0 yields O = NaN and LSE = -inf, as the reference does.
+ *
+ * seb_paged_decode is the split-K decode kernel: one warp per
+ * (query item, kv head, split of blocks_per_split blocks) with all query heads
+ * of the GQA group packed on one tensor-core tile, followed by a combine pass.
+ * It is correct for any query (decode or prefill rows alike) and is the fast
+ * path for q_len = 1 rows.
+ *   item_query[i]: token index of item i (NULL: item i is token i); tokens
+ *                  index q/out/lse, which hold total_query tokens;
+ *   item_row[i]:   its row (NULL: found by binary search over q_starts).
+ *   blocks_per_split <= 0 picks a default.
+ * workspace: at least seb_paged_decode_workspace_size(...) bytes, 16-byte aligned.
+ */
+SEB_API int64_t seb_paged_decode_workspace_size(int32_t num_items, int32_t num_q_heads,
+                                        int32_t num_kv_heads, int32_t head_dim,
+                                        int64_t max_blocks, int32_t blocks_per_split);
+
+SEB_API int seb_paged_decode(const void* q, int64_t q_stride_token, int64_t q_stride_head,
+                     const void* k_cache, const void* v_cache, int64_t num_blocks,
+                     const int32_t* block_table, int64_t block_table_stride, int64_t max_blocks,
+                     const int32_t* q_starts, const int32_t* k_lens, const int32_t* q_pos_offsets,
+                     int32_t num_rows, int32_t total_query, const int32_t* item_query,
+                     const int32_t* item_row, int32_t num_items, int32_t num_q_heads, int32_t num_kv_heads,
+                     int32_t head_dim, int32_t dtype, float scale, int32_t is_causal,
+                     int32_t blocks_per_split, void* out, int64_t out_stride_token,
+                     int64_t out_stride_head, float* lse, int64_t lse_stride_token,
+                     void* workspace, int64_t workspace_bytes, int32_t* err, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SERVING_ENGINE_B200_H */

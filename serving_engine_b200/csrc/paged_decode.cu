@@ -1,0 +1,736 @@
+// Split-K paged decode attention for sm_100a.
+//
+// Replaces the decode use (q_len = 1) of the reference's Triton kernel
+// paged_flash_fwd_kernel (serving_engine/paged_attention_kernel.py:16-122), which
+// runs one program per (16-query tile, row, q-head), re-reads the KV of a kv head
+// once per q-head of its GQA group and walks a row's whole context serially.
+//
+// Design (one warp = one work item (query item, kv head, split)):
+//   * A split is <= 32 consecutive 16-token blocks of the row; the warp keeps the
+//     split's block ids in one register per lane and streams each block's K and
+//     V rows (16 + 16 rows of head_dim elements, one 1-D bulk async copy per lane)
+//     through a STAGES-deep shared-memory ring completed on mbarriers.
+//   * All query heads of the GQA group share each KV tile: the 16 keys of a block
+//     are the M dimension of an m16n8k16 tensor-core tile and the (<= 8) heads of
+//     the group its N dimension, so S^T = K Q^T and O^T += V^T P^T each take
+//     head_dim/16 MMAs per block; P^T is moved from the accumulator layout to the
+//     operand layout with movmatrix. KV is read from HBM exactly once.
+//   * Online softmax in the log2 domain; per-split (m, l, O) go to a workspace
+//     and a combine pass merges splits. Items with one split write O/LSE directly.
+//
+// fp32 (and any shape the tensor-core path does not cover) runs a CUDA-core
+// variant with the same work decomposition and workspace format.
+//
+// Roofline: HBM. Algorithmic bytes = sum_items k_len * num_kv_heads * head_dim *
+// 2 (K and V) * elem; each KV byte is read once regardless of the group size.
+#include "seb_common.cuh"
+
+#include <cmath>
+
+namespace seb {
+namespace {
+
+constexpr float kLn2 = 0.69314718055994530942f;
+constexpr float kLog2e = 1.44269504088896340736f;
+constexpr unsigned kFull = 0xffffffffu;
+constexpr int kMaxBps = 32;  // blocks per split: one block id per lane
+
+struct DecodeParams {
+  const char* q;
+  int64_t q_st, q_sh;  // elements
+  const char* k_cache;
+  const char* v_cache;
+  int64_t num_blocks;
+  const int32_t* block_table;
+  int64_t bt_stride;
+  int64_t max_blocks;
+  const int32_t* q_starts;
+  const int32_t* k_lens;
+  const int32_t* q_pos;
+  int32_t num_rows;
+  int32_t total_query;
+  const int32_t* item_query;
+  const int32_t* item_row;
+  int32_t num_items;
+  int32_t hq, hkv, group;
+  float scale_log2;
+  int32_t causal;
+  int32_t bps, max_splits;
+  char* out;
+  int64_t o_st, o_sh;  // elements
+  float* lse;
+  int64_t lse_st;
+  float* ws_o;   // [items][hq][max_splits][D]
+  float* ws_ml;  // [items][hq][max_splits][2]  (m in log2 units, l)
+  int32_t* err;
+};
+
+struct ItemInfo {
+  int qtok, row, k_len, n_vis, nblk, n_splits;
+  bool ok;
+};
+
+// Last row r with q_starts[r] <= qtok (rows with q_len = 0 share the start of
+// the next row, so "last" picks the row that owns the token).
+__device__ __forceinline__ int find_row(const DecodeParams& p, int qtok) {
+  int lo = 0, hi = p.num_rows - 1, ans = 0;
+  while (lo <= hi) {
+    const int mid = (lo + hi) >> 1;
+    if (__ldg(p.q_starts + mid) <= qtok) {
+      ans = mid;
+      lo = mid + 1;
+    } else {
+      hi = mid - 1;
+    }
+  }
+  return ans;
+}
+
+// Keys visible to the item's query, following paged_attention_kernel.py:79-109:
+// the reference visits ceil(k_len/16) blocks, zero-pads keys past k_len inside the
+// last block (boundary-checked loads) and, when causal, drops keys after the
+// query's logical position (the -1e6 bias underflows exp to exactly 0).
+__device__ __forceinline__ ItemInfo item_info(const DecodeParams& p, int item) {
+  ItemInfo it;
+  it.ok = true;
+  it.qtok = p.item_query ? __ldg(p.item_query + item) : item;
+  if (it.qtok < 0 || it.qtok >= p.total_query) {
+    it.ok = false;
+    it.row = it.k_len = it.n_vis = it.nblk = it.n_splits = 0;
+    return it;
+  }
+  it.row = p.item_row ? __ldg(p.item_row + item) : find_row(p, it.qtok);
+  if (it.row < 0 || it.row >= p.num_rows) {
+    it.ok = false;
+    it.k_len = it.n_vis = it.nblk = it.n_splits = 0;
+    return it;
+  }
+  it.k_len = max(__ldg(p.k_lens + it.row), 0);
+  const int q_idx = __ldg(p.q_pos + it.row) + (it.qtok - __ldg(p.q_starts + it.row));
+  const int ceil16 = (it.k_len + 15) & ~15;
+  int nvis = p.causal ? min(ceil16, q_idx + 1) : ceil16;
+  nvis = max(nvis, 0);
+  int nblk = (nvis + 15) >> 4;
+  if (nblk > p.max_blocks) {
+    nblk = (int)p.max_blocks;
+    nvis = nblk * 16;
+  }
+  it.n_vis = nvis;
+  it.nblk = nblk;
+  it.n_splits = (nblk + p.bps - 1) / p.bps;
+  return it;
+}
+
+__device__ __forceinline__ void report_item(const DecodeParams& p, const ItemInfo& it, int lane) {
+  if (lane != 0) return;
+  if (!it.ok) atomic_or_err(p.err, SEB_ERRBIT_META);
+  else if ((int64_t)((it.k_len + 15) >> 4) > p.max_blocks) atomic_or_err(p.err, SEB_ERRBIT_KLEN);
+}
+
+// Block ids of blocks [b0, b0 + nb) of the row, one per lane; -1 when out of range.
+__device__ __forceinline__ int load_block_ids(const DecodeParams& p, const ItemInfo& it, int b0,
+                                              int nb, int lane) {
+  int bid = -1;
+  if (lane < nb) {
+    bid = __ldg(p.block_table + (int64_t)it.row * p.bt_stride + b0 + lane);
+    if (bid < 0 || (int64_t)bid >= p.num_blocks) {
+      atomic_or_err(p.err, SEB_ERRBIT_BLOCK_ID);
+      bid = -1;
+    }
+  }
+  return bid;
+}
+
+// --------------------------------------------------------------------------
+// Tensor-core path (fp16 / bf16).
+// --------------------------------------------------------------------------
+template <int D>
+struct MmaTile {
+  static constexpr int kRowBytes = D * 2;
+  static constexpr int kPitch = kRowBytes + 16;  // 16-byte skew: conflict-free ldmatrix
+  static constexpr int kTile = 16 * kPitch;      // one 16-row K or V tile
+  static constexpr int kStage = 2 * kTile;
+};
+
+template <int WARPS, int STAGES>
+constexpr int bar_bytes() {
+  return ((WARPS * STAGES * 8 + 127) / 128) * 128;
+}
+
+template <typename T, int D, int NTH, int STAGES, int WARPS>
+__global__ void __launch_bounds__(WARPS * 32) decode_mma_kernel(const DecodeParams p) {
+  using Tile = MmaTile<D>;
+  constexpr int KS = D / 16;
+  extern __shared__ __align__(128) char smem[];
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int g = lane >> 2;
+  const int t = lane & 3;
+
+  const int64_t w = (int64_t)blockIdx.x * WARPS + warp;
+  const int split = (int)(w % p.max_splits);
+  const int64_t tmp = w / p.max_splits;
+  const int kvh = (int)(tmp % p.hkv);
+  const int64_t item = tmp / p.hkv;
+  if (item >= p.num_items) return;
+
+  const ItemInfo it = item_info(p, (int)item);
+  if (split == 0 && kvh == 0) report_item(p, it, lane);
+  if (!it.ok) return;
+  if (split >= max(it.n_splits, 1)) return;
+  const int b0 = split * p.bps;
+  const int nb = min(p.bps, it.nblk - b0);  // <= 0 only when the row has no keys
+  const int bid_reg = load_block_ids(p, it, b0, max(nb, 0), lane);
+
+  // Q^T as the B operand (k = head dims, n = heads of the group), kept in registers.
+  uint32_t qf[KS][NTH][2];
+  {
+    const T* qbase = reinterpret_cast<const T*>(p.q) + (int64_t)it.qtok * p.q_st;
+#pragma unroll
+    for (int nt = 0; nt < NTH; ++nt) {
+      const int gh = nt * 8 + g;
+      const bool live = gh < p.group;
+      const T* qp = qbase + (int64_t)(kvh * p.group + (live ? gh : 0)) * p.q_sh;
+#pragma unroll
+      for (int ks = 0; ks < KS; ++ks) {
+        qf[ks][nt][0] = live ? *reinterpret_cast<const uint32_t*>(qp + ks * 16 + 2 * t) : 0u;
+        qf[ks][nt][1] = live ? *reinterpret_cast<const uint32_t*>(qp + ks * 16 + 8 + 2 * t) : 0u;
+      }
+    }
+  }
+
+  char* ring = smem + bar_bytes<WARPS, STAGES>() + warp * STAGES * Tile::kStage;
+  const uint32_t bar0 = smem_u32(smem) + warp * STAGES * 8;
+  if (lane == 0) {
+#pragma unroll
+    for (int s = 0; s < STAGES; ++s) mbar_init(bar0 + 8 * s, 1);
+    fence_mbar_init();
+  }
+  __syncwarp();
+
+  const char* kc = p.k_cache;
+  const char* vc = p.v_cache;
+  // Stage block j (relative to b0) into ring slot j % STAGES.
+  auto issue = [&](int j) {
+    const int s = j % STAGES;
+    const int blk = b0 + j;
+    const int bid = __shfl_sync(kFull, bid_reg, j);
+    const int vis = min(16, it.n_vis - blk * 16);
+    const int real = min(vis, it.k_len - blk * 16);
+    const int ncopy = bid >= 0 ? real : 0;
+    char* st = ring + s * Tile::kStage;
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) mbar_arrive_expect_tx(bar0 + 8 * s, (uint32_t)(ncopy * 2 * Tile::kRowBytes));
+    __syncwarp();
+    const int r = lane & 15;
+    const int isv = lane >> 4;
+    char* dst = st + isv * Tile::kTile + r * Tile::kPitch;
+    if (r < ncopy) {
+      const char* src = (isv ? vc : kc) +
+                        (((int64_t)bid * 16 + r) * p.hkv + kvh) * (int64_t)Tile::kRowBytes;
+      bulk_g2s(smem_u32(dst), src, Tile::kRowBytes, bar0 + 8 * s);
+    } else if (isv) {
+      // Zero V rows of keys that are padding or unreadable, so P = 0 (masked) or
+      // P = exp(-m) (phantom key, score 0) multiplies exact zeros.
+#pragma unroll
+      for (int c = 0; c < Tile::kRowBytes; c += 16)
+        *reinterpret_cast<uint4*>(dst + c) = make_uint4(0u, 0u, 0u, 0u);
+    }
+  };
+
+  float m_run[NTH][2], l_part[NTH][2];
+  float oacc[KS][NTH][4];
+#pragma unroll
+  for (int nt = 0; nt < NTH; ++nt) {
+    m_run[nt][0] = m_run[nt][1] = -INFINITY;
+    l_part[nt][0] = l_part[nt][1] = 0.f;
+#pragma unroll
+    for (int mt = 0; mt < KS; ++mt) oacc[mt][nt][0] = oacc[mt][nt][1] = oacc[mt][nt][2] = oacc[mt][nt][3] = 0.f;
+  }
+
+  const int npro = min(STAGES, max(nb, 0));
+  for (int j = 0; j < npro; ++j) issue(j);
+  __syncwarp();
+
+  bool timed_out = false;
+  for (int j = 0; j < nb; ++j) {
+    const int s = j % STAGES;
+    if (!mbar_wait_bounded(bar0 + 8 * s, (uint32_t)((j / STAGES) & 1))) {
+      timed_out = true;
+      // Drain the copies still in flight (bounded) before leaving the CTA.
+      for (int jj = j + 1; jj < min(j + STAGES, nb); ++jj)
+        mbar_wait_bounded(bar0 + 8 * (jj % STAGES), (uint32_t)((jj / STAGES) & 1), 1u << 16);
+      break;
+    }
+    const char* sk = ring + s * Tile::kStage;
+    const char* sv = sk + Tile::kTile;
+
+    // S^T = K Q^T : 16 keys x (8*NTH) heads, fp32 accumulate.
+    float sacc[NTH][4];
+#pragma unroll
+    for (int nt = 0; nt < NTH; ++nt) sacc[nt][0] = sacc[nt][1] = sacc[nt][2] = sacc[nt][3] = 0.f;
+    const uint32_t kaddr = smem_u32(sk + (lane & 15) * Tile::kPitch + (lane >> 4) * 16);
+#pragma unroll
+    for (int ks = 0; ks < KS; ++ks) {
+      uint32_t a0, a1, a2, a3;
+      ldmatrix_x4(kaddr + ks * 32, a0, a1, a2, a3);
+#pragma unroll
+      for (int nt = 0; nt < NTH; ++nt) Mma<T>::run(sacc[nt], a0, a1, a2, a3, qf[ks][nt][0], qf[ks][nt][1]);
+    }
+
+    // Scale into the log2 domain, mask, online softmax per head column. A block
+    // whose id was out of range was not copied: all of its keys are masked.
+    const bool bad = __shfl_sync(kFull, bid_reg, j) < 0;
+    const int key0 = (b0 + j) * 16 + g;
+    float corr[NTH][2];
+#pragma unroll
+    for (int nt = 0; nt < NTH; ++nt) {
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const int key = key0 + (c >> 1) * 8;
+        float x = sacc[nt][c] * p.scale_log2;
+        if (bad || key >= it.n_vis) x = -INFINITY;
+        else if (key >= it.k_len) x = 0.f;  // zero-padded key of the last block
+        sacc[nt][c] = x;
+      }
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        float mb = fmaxf(sacc[nt][h], sacc[nt][h + 2]);
+        mb = fmaxf(mb, __shfl_xor_sync(kFull, mb, 4));
+        mb = fmaxf(mb, __shfl_xor_sync(kFull, mb, 8));
+        mb = fmaxf(mb, __shfl_xor_sync(kFull, mb, 16));
+        const float m_new = fmaxf(m_run[nt][h], mb);
+        const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
+        const float cr = exp2f(m_run[nt][h] - m_use);
+        const float p0 = exp2f(sacc[nt][h] - m_use);
+        const float p1 = exp2f(sacc[nt][h + 2] - m_use);
+        l_part[nt][h] = l_part[nt][h] * cr + p0 + p1;
+        m_run[nt][h] = m_new;
+        corr[nt][h] = cr;
+        sacc[nt][h] = p0;
+        sacc[nt][h + 2] = p1;
+      }
+    }
+#pragma unroll
+    for (int mt = 0; mt < KS; ++mt)
+#pragma unroll
+      for (int nt = 0; nt < NTH; ++nt) {
+        oacc[mt][nt][0] *= corr[nt][0];
+        oacc[mt][nt][1] *= corr[nt][1];
+        oacc[mt][nt][2] *= corr[nt][0];
+        oacc[mt][nt][3] *= corr[nt][1];
+      }
+
+    // P^T (k = keys, n = heads) operand fragments.
+    uint32_t pb0[NTH], pb1[NTH];
+#pragma unroll
+    for (int nt = 0; nt < NTH; ++nt) {
+      pb0[nt] = movmatrix_trans(Mma<T>::pack(sacc[nt][0], sacc[nt][1]));
+      pb1[nt] = movmatrix_trans(Mma<T>::pack(sacc[nt][2], sacc[nt][3]));
+    }
+
+    // O^T += V^T P^T : head_dim x heads.
+    const uint32_t vaddr =
+        smem_u32(sv + ((lane & 7) + (lane >> 4) * 8) * Tile::kPitch + ((lane >> 3) & 1) * 16);
+#pragma unroll
+    for (int mt = 0; mt < KS; ++mt) {
+      uint32_t a0, a1, a2, a3;
+      ldmatrix_x4_trans(vaddr + mt * 32, a0, a1, a2, a3);
+#pragma unroll
+      for (int nt = 0; nt < NTH; ++nt) Mma<T>::run(oacc[mt][nt], a0, a1, a2, a3, pb0[nt], pb1[nt]);
+    }
+    __syncwarp();
+    if (j + STAGES < nb) {
+      issue(j + STAGES);
+      __syncwarp();
+    }
+  }
+  if (timed_out) {
+    if (lane == 0) atomic_or_err(p.err, SEB_ERRBIT_TIMEOUT);
+    return;
+  }
+
+  float l_tot[NTH][2];
+#pragma unroll
+  for (int nt = 0; nt < NTH; ++nt)
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      float l = l_part[nt][h];
+      l += __shfl_xor_sync(kFull, l, 4);
+      l += __shfl_xor_sync(kFull, l, 8);
+      l += __shfl_xor_sync(kFull, l, 16);
+      l_tot[nt][h] = l;
+    }
+
+  if (it.n_splits <= 1) {
+    T* obase = reinterpret_cast<T*>(p.out) + (int64_t)it.qtok * p.o_st;
+#pragma unroll
+    for (int nt = 0; nt < NTH; ++nt)
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int gh = nt * 8 + 2 * t + h;
+        if (gh >= p.group) continue;
+        const int qh = kvh * p.group + gh;
+        T* op = obase + (int64_t)qh * p.o_sh;
+#pragma unroll
+        for (int mt = 0; mt < KS; ++mt) {
+          op[mt * 16 + g] = Elem<T>::from_float(oacc[mt][nt][h] / l_tot[nt][h]);
+          op[mt * 16 + g + 8] = Elem<T>::from_float(oacc[mt][nt][h + 2] / l_tot[nt][h]);
+        }
+        if (g == 0) p.lse[(int64_t)it.qtok * p.lse_st + qh] = m_run[nt][h] * kLn2 + logf(l_tot[nt][h]);
+      }
+  } else {
+#pragma unroll
+    for (int nt = 0; nt < NTH; ++nt)
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int gh = nt * 8 + 2 * t + h;
+        if (gh >= p.group) continue;
+        const int qh = kvh * p.group + gh;
+        const int64_t slot = ((item * p.hq + qh) * p.max_splits + split);
+        float* wo = p.ws_o + slot * D;
+#pragma unroll
+        for (int mt = 0; mt < KS; ++mt) {
+          wo[mt * 16 + g] = oacc[mt][nt][h];
+          wo[mt * 16 + g + 8] = oacc[mt][nt][h + 2];
+        }
+        if (g == 0) {
+          p.ws_ml[slot * 2] = m_run[nt][h];
+          p.ws_ml[slot * 2 + 1] = l_tot[nt][h];
+        }
+      }
+  }
+}
+
+// --------------------------------------------------------------------------
+// CUDA-core path (fp32, or shapes without a tensor-core kernel). Same work
+// decomposition; each lane owns head dims lane + 32*i; keys are visited one at
+// a time with a full-warp dot-product reduction.
+// --------------------------------------------------------------------------
+template <typename T, int D, int GMAX, int WARPS>
+__global__ void __launch_bounds__(WARPS * 32) decode_simt_kernel(const DecodeParams p) {
+  constexpr int DL = D / 32;
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int64_t w = (int64_t)blockIdx.x * WARPS + warp;
+  const int split = (int)(w % p.max_splits);
+  const int64_t tmp = w / p.max_splits;
+  const int kvh = (int)(tmp % p.hkv);
+  const int64_t item = tmp / p.hkv;
+  if (item >= p.num_items) return;
+  const ItemInfo it = item_info(p, (int)item);
+  if (split == 0 && kvh == 0) report_item(p, it, lane);
+  if (!it.ok) return;
+  if (split >= max(it.n_splits, 1)) return;
+  const int b0 = split * p.bps;
+  const int nb = min(p.bps, it.nblk - b0);
+  const int bid_reg = load_block_ids(p, it, b0, max(nb, 0), lane);
+
+  float qv[GMAX][DL];
+  const T* qbase = reinterpret_cast<const T*>(p.q) + (int64_t)it.qtok * p.q_st;
+#pragma unroll
+  for (int gh = 0; gh < GMAX; ++gh)
+#pragma unroll
+    for (int i = 0; i < DL; ++i)
+      qv[gh][i] = gh < p.group
+                      ? Elem<T>::to_float(qbase[(int64_t)(kvh * p.group + gh) * p.q_sh + lane + 32 * i])
+                      : 0.f;
+
+  float m[GMAX], l[GMAX], o[GMAX][DL];
+#pragma unroll
+  for (int gh = 0; gh < GMAX; ++gh) {
+    m[gh] = -INFINITY;
+    l[gh] = 0.f;
+#pragma unroll
+    for (int i = 0; i < DL; ++i) o[gh][i] = 0.f;
+  }
+
+  const T* kc = reinterpret_cast<const T*>(p.k_cache);
+  const T* vc = reinterpret_cast<const T*>(p.v_cache);
+  for (int j = 0; j < nb; ++j) {
+    const int blk = b0 + j;
+    const int bid = __shfl_sync(kFull, bid_reg, j);
+    const int vis = min(16, it.n_vis - blk * 16);
+    const int real = bid >= 0 ? min(vis, it.k_len - blk * 16) : 0;
+    for (int r = 0; r < vis; ++r) {
+      float kv[DL], vv[DL];
+      if (r < real) {
+        const int64_t off = (((int64_t)bid * 16 + r) * p.hkv + kvh) * D + lane;
+#pragma unroll
+        for (int i = 0; i < DL; ++i) {
+          kv[i] = Elem<T>::to_float(kc[off + 32 * i]);
+          vv[i] = Elem<T>::to_float(vc[off + 32 * i]);
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < DL; ++i) kv[i] = vv[i] = 0.f;
+      }
+      const bool readable = (r < real) || (bid >= 0);
+#pragma unroll
+      for (int gh = 0; gh < GMAX; ++gh) {
+        if (gh >= p.group) break;
+        float sdot = 0.f;
+#pragma unroll
+        for (int i = 0; i < DL; ++i) sdot = fmaf(qv[gh][i], kv[i], sdot);
+#pragma unroll
+        for (int off = 16; off >= 1; off >>= 1) sdot += __shfl_xor_sync(kFull, sdot, off);
+        // unreadable block (bad id): treated as masked
+        const float x = readable ? sdot * p.scale_log2 : -INFINITY;
+        const float m_new = fmaxf(m[gh], x);
+        const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
+        const float cr = exp2f(m[gh] - m_use);
+        const float pr = exp2f(x - m_use);
+        l[gh] = l[gh] * cr + pr;
+#pragma unroll
+        for (int i = 0; i < DL; ++i) o[gh][i] = fmaf(pr, vv[i], o[gh][i] * cr);
+        m[gh] = m_new;
+      }
+    }
+  }
+
+  if (it.n_splits <= 1) {
+    T* obase = reinterpret_cast<T*>(p.out) + (int64_t)it.qtok * p.o_st;
+#pragma unroll
+    for (int gh = 0; gh < GMAX; ++gh) {
+      if (gh >= p.group) break;
+      const int qh = kvh * p.group + gh;
+#pragma unroll
+      for (int i = 0; i < DL; ++i)
+        obase[(int64_t)qh * p.o_sh + lane + 32 * i] = Elem<T>::from_float(o[gh][i] / l[gh]);
+      if (lane == 0) p.lse[(int64_t)it.qtok * p.lse_st + qh] = m[gh] * kLn2 + logf(l[gh]);
+    }
+  } else {
+#pragma unroll
+    for (int gh = 0; gh < GMAX; ++gh) {
+      if (gh >= p.group) break;
+      const int qh = kvh * p.group + gh;
+      const int64_t slot = ((item * p.hq + qh) * p.max_splits + split);
+#pragma unroll
+      for (int i = 0; i < DL; ++i) p.ws_o[slot * D + lane + 32 * i] = o[gh][i];
+      if (lane == 0) {
+        p.ws_ml[slot * 2] = m[gh];
+        p.ws_ml[slot * 2 + 1] = l[gh];
+      }
+    }
+  }
+}
+
+// --------------------------------------------------------------------------
+// Combine pass: one warp per (item, q head) with >= 2 splits.
+// --------------------------------------------------------------------------
+template <typename T, int D>
+__global__ void __launch_bounds__(128) decode_combine_kernel(const DecodeParams p) {
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int64_t w = (int64_t)blockIdx.x * 4 + warp;
+  const int64_t item = w / p.hq;
+  const int qh = (int)(w % p.hq);
+  if (item >= p.num_items) return;
+  const ItemInfo it = item_info(p, (int)item);
+  if (!it.ok || it.n_splits <= 1) return;
+  const int64_t base = (item * p.hq + qh) * p.max_splits;
+  const float* ml = p.ws_ml + base * 2;
+  float mx = -INFINITY;
+  for (int s = lane; s < it.n_splits; s += 32) mx = fmaxf(mx, ml[2 * s]);
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(kFull, mx, off));
+  const float m_use = (mx == -INFINITY) ? 0.f : mx;
+  float lsum = 0.f;
+  for (int s = lane; s < it.n_splits; s += 32) lsum += ml[2 * s + 1] * exp2f(ml[2 * s] - m_use);
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) lsum += __shfl_xor_sync(kFull, lsum, off);
+
+  T* op = reinterpret_cast<T*>(p.out) + (int64_t)it.qtok * p.o_st + (int64_t)qh * p.o_sh;
+  const float* wo = p.ws_o + base * D;
+#pragma unroll
+  for (int i = 0; i < D / 32; ++i) {
+    float acc = 0.f;
+    for (int s = 0; s < it.n_splits; ++s) acc = fmaf(exp2f(ml[2 * s] - m_use), wo[(int64_t)s * D + lane + 32 * i], acc);
+    op[lane + 32 * i] = Elem<T>::from_float(acc / lsum);
+  }
+  if (lane == 0) p.lse[(int64_t)it.qtok * p.lse_st + qh] = mx * kLn2 + logf(lsum);
+}
+
+// ------------------------------------------------------------------ launching
+constexpr int kMmaWarps = 4;
+constexpr int kMmaStages = 3;
+constexpr int kSimtWarps = 4;
+
+int choose_bps(int num_items, int hkv, int64_t max_blocks, int requested) {
+  if (requested > 0) return requested > kMaxBps ? kMaxBps : requested;
+  // Aim for about four waves of 8 resident warps per SM, assuming rows fill
+  // about half of the block-table width; keep >= 8 blocks so the copy ring
+  // has work to pipeline.
+  const double est_blocks = 0.5 * (double)num_items * hkv * (double)max_blocks;
+  const double slots = (double)num_sms() * 8.0 * 4.0;
+  int bps = (int)std::ceil(est_blocks / slots);
+  if (bps < 8) bps = 8;
+  if (bps > kMaxBps) bps = kMaxBps;
+  return bps;
+}
+
+template <typename T, int D, int NTH>
+int launch_mma(const DecodeParams& p, int64_t n_warps, cudaStream_t s) {
+  constexpr int smem = bar_bytes<kMmaWarps, kMmaStages>() + kMmaWarps * kMmaStages * MmaTile<D>::kStage;
+  auto kern = decode_mma_kernel<T, D, NTH, kMmaStages, kMmaWarps>;
+  static bool attr_set[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+    SEB_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    attr_set[dev] = true;
+  }
+  const int64_t grid = (n_warps + kMmaWarps - 1) / kMmaWarps;
+  kern<<<(unsigned)grid, kMmaWarps * 32, smem, s>>>(p);
+  return launch_status("decode_mma_kernel");
+}
+
+template <typename T, int D, int GMAX>
+int launch_simt(const DecodeParams& p, int64_t n_warps, cudaStream_t s) {
+  const int64_t grid = (n_warps + kSimtWarps - 1) / kSimtWarps;
+  decode_simt_kernel<T, D, GMAX, kSimtWarps><<<(unsigned)grid, kSimtWarps * 32, 0, s>>>(p);
+  return launch_status("decode_simt_kernel");
+}
+
+template <typename T, int D>
+int launch_simt_g(const DecodeParams& p, int64_t n_warps, cudaStream_t s) {
+  if (p.group <= 1) return launch_simt<T, D, 1>(p, n_warps, s);
+  if (p.group <= 2) return launch_simt<T, D, 2>(p, n_warps, s);
+  if (p.group <= 4) return launch_simt<T, D, 4>(p, n_warps, s);
+  if (p.group <= 8) return launch_simt<T, D, 8>(p, n_warps, s);
+  return launch_simt<T, D, 16>(p, n_warps, s);
+}
+
+template <typename T, int D>
+int launch_typed(const DecodeParams& p, int64_t n_warps, bool tensor_core, cudaStream_t s) {
+  int rc;
+  if constexpr (sizeof(T) == 2) {
+    if (tensor_core) {
+      rc = p.group <= 8 ? launch_mma<T, D, 1>(p, n_warps, s) : launch_mma<T, D, 2>(p, n_warps, s);
+    } else {
+      rc = launch_simt_g<T, D>(p, n_warps, s);
+    }
+  } else {
+    rc = launch_simt_g<T, D>(p, n_warps, s);
+  }
+  if (rc != SEB_OK || p.max_splits <= 1) return rc;
+  const int64_t combos = (int64_t)p.num_items * p.hq;
+  decode_combine_kernel<T, D><<<(unsigned)((combos + 3) / 4), 128, 0, s>>>(p);
+  return launch_status("decode_combine_kernel");
+}
+
+template <typename T>
+int launch_dim(const DecodeParams& p, int D, int64_t n_warps, bool tc, cudaStream_t s) {
+  switch (D) {
+    case 64: return launch_typed<T, 64>(p, n_warps, tc, s);
+    case 128: return launch_typed<T, 128>(p, n_warps, tc, s);
+    case 256: return launch_typed<T, 256>(p, n_warps, tc, s);
+    default: set_error("head_dim %d not supported (64, 128, 256)", D); return SEB_EUNSUPPORTED;
+  }
+}
+
+}  // namespace
+}  // namespace seb
+
+extern "C" int64_t seb_paged_decode_workspace_size(int32_t num_items, int32_t num_q_heads,
+                                                   int32_t num_kv_heads, int32_t head_dim,
+                                                   int64_t max_blocks, int32_t blocks_per_split) {
+  using namespace seb;
+  if (num_items <= 0 || num_q_heads <= 0 || num_kv_heads <= 0 || head_dim <= 0 || max_blocks <= 0)
+    return 0;
+  const int bps = choose_bps(num_items, num_kv_heads, max_blocks, blocks_per_split);
+  const int64_t max_splits = (max_blocks + bps - 1) / bps;
+  if (max_splits <= 1) return 0;
+  return (int64_t)num_items * num_q_heads * max_splits * (head_dim + 2) * (int64_t)sizeof(float);
+}
+
+extern "C" int seb_paged_decode(const void* q, int64_t q_stride_token, int64_t q_stride_head,
+                                const void* k_cache, const void* v_cache, int64_t num_blocks,
+                                const int32_t* block_table, int64_t block_table_stride,
+                                int64_t max_blocks, const int32_t* q_starts, const int32_t* k_lens,
+                                const int32_t* q_pos_offsets, int32_t num_rows, int32_t total_query,
+                                const int32_t* item_query, const int32_t* item_row,
+                                int32_t num_items, int32_t num_q_heads, int32_t num_kv_heads,
+                                int32_t head_dim, int32_t dtype, float scale, int32_t is_causal,
+                                int32_t blocks_per_split, void* out, int64_t out_stride_token,
+                                int64_t out_stride_head, float* lse, int64_t lse_stride_token,
+                                void* workspace, int64_t workspace_bytes, int32_t* err,
+                                void* stream) {
+  using namespace seb;
+  clear_error();
+  const int es = elem_size(dtype);
+  SEB_CHECK_ARG(es > 0, "seb_paged_decode: unknown dtype %d", dtype);
+  SEB_CHECK_ARG(num_items >= 0 && num_rows >= 0 && total_query >= 0, "seb_paged_decode: negative count");
+  if (num_items == 0) return SEB_OK;
+  SEB_CHECK_ARG(num_rows > 0, "seb_paged_decode: items given but no rows");
+  SEB_CHECK_ARG(num_q_heads > 0 && num_kv_heads > 0 && num_q_heads % num_kv_heads == 0,
+                "seb_paged_decode: num_q_heads (%d) must be a positive multiple of num_kv_heads (%d)",
+                num_q_heads, num_kv_heads);
+  const int group = num_q_heads / num_kv_heads;
+  SEB_CHECK_ARG(group <= 16, "seb_paged_decode: GQA group %d > 16 not supported", group);
+  SEB_CHECK_ARG(q && k_cache && v_cache && block_table && q_starts && k_lens && q_pos_offsets && out && lse,
+                "seb_paged_decode: NULL pointer argument");
+  SEB_CHECK_ARG(num_blocks > 0 && max_blocks > 0 && block_table_stride >= max_blocks,
+                "seb_paged_decode: bad block table shape (num_blocks %lld, max_blocks %lld, stride %lld)",
+                (long long)num_blocks, (long long)max_blocks, (long long)block_table_stride);
+  SEB_CHECK_ARG(aligned(k_cache, 16) && aligned(v_cache, 16), "seb_paged_decode: KV pool not 16-byte aligned");
+  const bool tc = (dtype != SEB_F32);
+  if (tc) {
+    SEB_CHECK_ARG(aligned(q, 4) && q_stride_token % 2 == 0 && q_stride_head % 2 == 0,
+                  "seb_paged_decode: q must be 4-byte aligned with even strides");
+  }
+
+  DecodeParams p;
+  p.q = static_cast<const char*>(q);
+  p.q_st = q_stride_token;
+  p.q_sh = q_stride_head;
+  p.k_cache = static_cast<const char*>(k_cache);
+  p.v_cache = static_cast<const char*>(v_cache);
+  p.num_blocks = num_blocks;
+  p.block_table = block_table;
+  p.bt_stride = block_table_stride;
+  p.max_blocks = max_blocks;
+  p.q_starts = q_starts;
+  p.k_lens = k_lens;
+  p.q_pos = q_pos_offsets;
+  p.num_rows = num_rows;
+  p.total_query = total_query;
+  p.item_query = item_query;
+  p.item_row = item_row;
+  p.num_items = num_items;
+  p.hq = num_q_heads;
+  p.hkv = num_kv_heads;
+  p.group = group;
+  p.scale_log2 = scale * kLog2e;
+  p.causal = is_causal ? 1 : 0;
+  p.bps = choose_bps(num_items, num_kv_heads, max_blocks, blocks_per_split);
+  p.max_splits = (int)((max_blocks + p.bps - 1) / p.bps);
+  p.out = static_cast<char*>(out);
+  p.o_st = out_stride_token;
+  p.o_sh = out_stride_head;
+  p.lse = lse;
+  p.lse_st = lse_stride_token;
+  p.err = err;
+  p.ws_o = nullptr;
+  p.ws_ml = nullptr;
+  if (p.max_splits > 1) {
+    const int64_t need = seb_paged_decode_workspace_size(num_items, num_q_heads, num_kv_heads, head_dim,
+                                                         max_blocks, blocks_per_split);
+    if (workspace == nullptr || workspace_bytes < need || !aligned(workspace, 16)) {
+      set_error("seb_paged_decode: workspace of %lld bytes (16-byte aligned) required, got %lld",
+                (long long)need, (long long)workspace_bytes);
+      return SEB_EWORKSPACE;
+    }
+    p.ws_o = static_cast<float*>(workspace);
+    p.ws_ml = p.ws_o + (int64_t)num_items * num_q_heads * p.max_splits * head_dim;
+  }
+  const int64_t n_warps = (int64_t)num_items * num_kv_heads * p.max_splits;
+  SEB_CHECK_ARG((n_warps + 3) / 4 < (1ll << 31), "seb_paged_decode: grid too large");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  switch (dtype) {
+    case SEB_BF16: return launch_dim<__nv_bfloat16>(p, head_dim, n_warps, tc, s);
+    case SEB_F16: return launch_dim<__half>(p, head_dim, n_warps, tc, s);
+    default: return launch_dim<float>(p, head_dim, n_warps, false, s);
+  }
+}

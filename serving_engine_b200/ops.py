@@ -1,0 +1,259 @@
+"""Tensor-level wrappers over the C ABI (device memory and streams from torch).
+
+Each op validates shapes, dtypes and devices on the host, without a device
+sync, and enqueues its kernel on the current torch CUDA stream. Kernels report
+out-of-range indices met at run time through a per-device int32 error word,
+which ``check_device_errors()`` reads back (one sync) and raises on.
+"""
+from __future__ import annotations
+
+import os
+import threading
+
+import torch
+
+from . import _lib
+from ._lib import SEB_BF16, SEB_F16, SEB_F32, check, lib
+
+BLOCK_SIZE = 16  # serving_engine/block.py:7
+
+_DTYPES = {torch.float32: SEB_F32, torch.float16: SEB_F16, torch.bfloat16: SEB_BF16}
+
+_state = threading.local()
+# Number of kernels each op enqueued so far (host-side count, read by bench.py).
+LAUNCHES = [0]
+_err_words: dict[int, torch.Tensor] = {}
+_workspaces: dict[int, torch.Tensor] = {}
+
+# SEB_DEBUG=1 checks the device error word after every op (one sync per op).
+DEBUG = os.environ.get("SEB_DEBUG", "0") not in ("", "0")
+
+
+def dtype_code(t: torch.Tensor) -> int:
+    try:
+        return _DTYPES[t.dtype]
+    except KeyError:
+        raise ValueError(f"unsupported dtype {t.dtype}; expected float32, float16 or bfloat16") from None
+
+
+def _require_cuda(name: str, *tensors: torch.Tensor) -> torch.device:
+    dev = tensors[0].device
+    if dev.type != "cuda":
+        raise ValueError(f"{name}: tensors must be on a CUDA device, got {dev}")
+    for t in tensors[1:]:
+        if t.device != dev:
+            raise ValueError(f"{name}: all tensors must be on {dev}, got {t.device}")
+    return dev
+
+
+def _stream(dev: torch.device) -> int:
+    return torch.cuda.current_stream(dev).cuda_stream
+
+
+def err_word(dev: torch.device) -> torch.Tensor:
+    """The device's int32 error word (created zeroed on first use)."""
+    idx = dev.index if dev.index is not None else torch.cuda.current_device()
+    w = _err_words.get(idx)
+    if w is None:
+        w = torch.zeros(1, dtype=torch.int32, device=torch.device("cuda", idx))
+        _err_words[idx] = w
+    return w
+
+
+def check_device_errors(dev: torch.device | None = None, reset: bool = True) -> None:
+    """Sync, read the error word and raise RuntimeError naming its bits."""
+    devs = [dev] if dev is not None else [torch.device("cuda", i) for i in list(_err_words)]
+    for d in devs:
+        w = err_word(d)
+        bits = int(w.item())
+        if reset:
+            w.zero_()
+        if bits:
+            raise RuntimeError(f"serving_engine_b200 kernel error on {d}: " + ", ".join(_lib.decode_errbits(bits)))
+
+
+def workspace(dev: torch.device, nbytes: int) -> torch.Tensor:
+    """A per-device scratch buffer of at least nbytes, grown on demand."""
+    idx = dev.index if dev.index is not None else torch.cuda.current_device()
+    ws = _workspaces.get(idx)
+    if ws is None or ws.numel() < nbytes:
+        ws = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=torch.device("cuda", idx))
+        _workspaces[idx] = ws
+    return ws
+
+
+def _after(dev: torch.device) -> None:
+    if DEBUG:
+        check_device_errors(dev)
+
+
+# ------------------------------------------------------------------ kv append
+def kv_append(k_new: torch.Tensor, v_new: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
+              slot_mapping: torch.Tensor) -> None:
+    """k_cache.view(-1, H, D)[slot_mapping] = k_new; same for V (one launch).
+
+    k_new, v_new: [n_tokens, H, D] with unit stride on D (any token/head strides).
+    k_cache, v_cache: [num_blocks, 16, H, D] contiguous. slot_mapping: int64 [n_tokens].
+    Equivalent to the two index_copy_ of _PagedKVCache.write (model_runner.py:21-32).
+    """
+    dev = _require_cuda("kv_append", k_new, v_new, k_cache, v_cache, slot_mapping)
+    if k_new.dim() != 3 or v_new.shape != k_new.shape:
+        raise ValueError(f"kv_append: k_new/v_new must both be [n_tokens, H, D], got {tuple(k_new.shape)} "
+                         f"and {tuple(v_new.shape)}")
+    n, h, d = k_new.shape
+    if k_cache.dim() != 4 or k_cache.shape[1] != BLOCK_SIZE or tuple(k_cache.shape[2:]) != (h, d):
+        raise ValueError(f"kv_append: k_cache must be [num_blocks, {BLOCK_SIZE}, {h}, {d}], got {tuple(k_cache.shape)}")
+    if v_cache.shape != k_cache.shape:
+        raise ValueError("kv_append: k_cache and v_cache shapes differ")
+    if not (k_cache.is_contiguous() and v_cache.is_contiguous()):
+        raise ValueError("kv_append: KV caches must be contiguous")
+    if not (k_new.dtype == v_new.dtype == k_cache.dtype == v_cache.dtype):
+        raise ValueError("kv_append: dtype mismatch between new K/V and the cache")
+    if k_new.stride(2) != 1 or v_new.stride(2) != 1:
+        raise ValueError("kv_append: new K/V must have unit stride on head_dim")
+    if slot_mapping.dtype != torch.int64 or slot_mapping.dim() != 1 or slot_mapping.numel() != n:
+        raise ValueError(f"kv_append: slot_mapping must be int64 [{n}]")
+    if not slot_mapping.is_contiguous():
+        slot_mapping = slot_mapping.contiguous()
+    st = lib().seb_kv_append(
+        k_new.data_ptr(), k_new.stride(0), k_new.stride(1),
+        v_new.data_ptr(), v_new.stride(0), v_new.stride(1),
+        n, slot_mapping.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(),
+        k_cache.shape[0], h, d, dtype_code(k_cache), err_word(dev).data_ptr(), _stream(dev))
+    check("seb_kv_append", st)
+    LAUNCHES[0] += 1
+    _after(dev)
+
+
+# ---------------------------------------------------------------- copy blocks
+def copy_blocks(kv_cache: torch.Tensor, src, dst) -> None:
+    """kv_cache[:, :, dst] = kv_cache[:, :, src] for the engine pool
+    [L, 2, num_blocks, 16, H, D] (model_runner.py:101-110), one launch.
+
+    src/dst: sequences of block ids or int64 tensors. dst ids must be distinct
+    and disjoint from src ids; host lists are validated here.
+    """
+    dev = _require_cuda("copy_blocks", kv_cache)
+    if kv_cache.dim() != 6 or kv_cache.shape[1] != 2 or kv_cache.shape[3] != BLOCK_SIZE:
+        raise ValueError(f"copy_blocks: pool must be [L, 2, num_blocks, {BLOCK_SIZE}, H, D], got {tuple(kv_cache.shape)}")
+    if not kv_cache.is_contiguous():
+        raise ValueError("copy_blocks: pool must be contiguous")
+    nb = kv_cache.shape[2]
+    src_t, dst_t = _block_ids(src, dev, "src"), _block_ids(dst, dev, "dst")
+    if src_t.numel() != dst_t.numel():
+        raise ValueError("copy_blocks: src and dst lengths differ")
+    if not isinstance(src, torch.Tensor) and not isinstance(dst, torch.Tensor):
+        s, d = list(src), list(dst)
+        if len(set(d)) != len(d):
+            raise ValueError("copy_blocks: duplicate dst block ids")
+        if set(s) & set(d):
+            raise ValueError("copy_blocks: a dst block is also a src block")
+        bad = [b for b in s + d if not 0 <= int(b) < nb]
+        if bad:
+            raise ValueError(f"copy_blocks: block ids out of range [0, {nb}): {bad[:8]}")
+    n = src_t.numel()
+    if n == 0:
+        return
+    block_bytes = BLOCK_SIZE * kv_cache.shape[4] * kv_cache.shape[5] * kv_cache.element_size()
+    layer_stride = kv_cache.stride(0) * kv_cache.element_size()
+    st = lib().seb_copy_blocks(kv_cache.data_ptr(), kv_cache.shape[0], layer_stride, nb, block_bytes,
+                               src_t.data_ptr(), dst_t.data_ptr(), n, err_word(dev).data_ptr(), _stream(dev))
+    check("seb_copy_blocks", st)
+    LAUNCHES[0] += 1
+    _after(dev)
+
+
+def _block_ids(x, dev: torch.device, name: str) -> torch.Tensor:
+    if isinstance(x, torch.Tensor):
+        if x.device != dev:
+            raise ValueError(f"copy_blocks: {name} must be on {dev}")
+        return x.to(torch.int64).contiguous()
+    return torch.tensor(list(x), dtype=torch.int64).pin_memory().to(dev, non_blocking=True)
+
+
+# --------------------------------------------------------------- paged decode
+def decode_workspace_bytes(num_items: int, num_q_heads: int, num_kv_heads: int, head_dim: int,
+                           max_blocks: int, blocks_per_split: int = 0) -> int:
+    return int(lib().seb_paged_decode_workspace_size(num_items, num_q_heads, num_kv_heads, head_dim,
+                                                     max_blocks, blocks_per_split))
+
+
+def paged_decode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, block_table: torch.Tensor,
+                 q_starts: torch.Tensor, k_lens: torch.Tensor, q_pos_offsets: torch.Tensor,
+                 num_q_heads: int, num_kv_heads: int, scale: float, is_causal: bool = True,
+                 item_query: torch.Tensor | None = None, item_row: torch.Tensor | None = None,
+                 out: torch.Tensor | None = None, lse: torch.Tensor | None = None,
+                 blocks_per_split: int = 0) -> tuple[torch.Tensor, torch.Tensor]:
+    """Split-K paged attention for the listed query items (default: every token).
+
+    q: [total_query, num_q_heads, D]; caches [num_blocks, 16, num_kv_heads, D];
+    block_table int32 [rows, max_blocks]; q_starts/k_lens/q_pos_offsets int32 [rows].
+    Returns (out like q, lse fp32 [total_query, num_q_heads]); rows of tokens that
+    are not items are left untouched.
+    """
+    dev = _require_cuda("paged_decode", q, k_cache, v_cache, block_table, q_starts, k_lens, q_pos_offsets)
+    if q.dim() != 3 or q.stride(2) != 1:
+        raise ValueError(f"paged_decode: q must be [total_query, heads, head_dim] with unit inner stride, got {tuple(q.shape)}")
+    total_q, hq, d = q.shape
+    if hq != num_q_heads:
+        raise ValueError(f"paged_decode: q has {hq} heads, num_q_heads={num_q_heads}")
+    if num_kv_heads <= 0 or num_q_heads % num_kv_heads:
+        raise ValueError(f"paged_decode: num_q_heads {num_q_heads} not a multiple of num_kv_heads {num_kv_heads}")
+    if k_cache.dim() != 4 or k_cache.shape[1] != BLOCK_SIZE or tuple(k_cache.shape[2:]) != (num_kv_heads, d):
+        raise ValueError(f"paged_decode: k_cache must be [num_blocks, {BLOCK_SIZE}, {num_kv_heads}, {d}], "
+                         f"got {tuple(k_cache.shape)}")
+    if v_cache.shape != k_cache.shape or not (k_cache.is_contiguous() and v_cache.is_contiguous()):
+        raise ValueError("paged_decode: k_cache and v_cache must be contiguous and of equal shape")
+    if not (q.dtype == k_cache.dtype == v_cache.dtype):
+        raise ValueError(f"paged_decode: dtype mismatch q {q.dtype}, cache {k_cache.dtype}")
+    for name, t in (("block_table", block_table), ("q_starts", q_starts), ("k_lens", k_lens),
+                    ("q_pos_offsets", q_pos_offsets)):
+        if t.dtype != torch.int32:
+            raise ValueError(f"paged_decode: {name} must be int32, got {t.dtype}")
+    rows = q_starts.numel()
+    if k_lens.numel() != rows or q_pos_offsets.numel() != rows:
+        raise ValueError("paged_decode: q_starts, k_lens and q_pos_offsets lengths differ")
+    if block_table.dim() != 2 or block_table.shape[0] != rows:
+        raise ValueError(f"paged_decode: block_table must be [{rows}, max_blocks], got {tuple(block_table.shape)}")
+    if block_table.stride(1) != 1:
+        block_table = block_table.contiguous()
+    q_starts, k_lens, q_pos_offsets = (t.contiguous() for t in (q_starts, k_lens, q_pos_offsets))
+    max_blocks = block_table.shape[1]
+    if item_query is not None:
+        item_query = item_query.to(torch.int32).contiguous()
+        num_items = item_query.numel()
+    else:
+        num_items = total_q
+    if item_row is not None:
+        item_row = item_row.to(torch.int32).contiguous()
+        if item_row.numel() != num_items:
+            raise ValueError("paged_decode: item_row length differs from the number of items")
+    if out is None:
+        out = torch.empty_like(q)
+    if lse is None:
+        lse = torch.empty((total_q, num_q_heads), dtype=torch.float32, device=dev)
+    if num_items == 0 or rows == 0 or max_blocks == 0:
+        if num_items and rows:
+            # no block table columns: every row has k_len 0 -> reference semantics O = NaN, LSE = -inf
+            out.fill_(float("nan"))
+            lse.fill_(float("-inf"))
+        return out, lse
+    ws_bytes = decode_workspace_bytes(num_items, num_q_heads, num_kv_heads, d, max_blocks, blocks_per_split)
+    ws = workspace(dev, ws_bytes)
+    st = lib().seb_paged_decode(
+        q.data_ptr(), q.stride(0), q.stride(1),
+        k_cache.data_ptr(), v_cache.data_ptr(), k_cache.shape[0],
+        block_table.data_ptr(), block_table.stride(0), max_blocks,
+        q_starts.data_ptr(), k_lens.data_ptr(), q_pos_offsets.data_ptr(),
+        rows, total_q,
+        item_query.data_ptr() if item_query is not None else None,
+        item_row.data_ptr() if item_row is not None else None,
+        num_items, num_q_heads, num_kv_heads, d, dtype_code(q),
+        float(scale), 1 if is_causal else 0, int(blocks_per_split),
+        out.data_ptr(), out.stride(0), out.stride(1),
+        lse.data_ptr(), lse.stride(0),
+        ws.data_ptr(), ws.numel(), err_word(dev).data_ptr(), _stream(dev))
+    check("seb_paged_decode", st)
+    LAUNCHES[0] += 2 if ws_bytes > 0 else 1  # split pass (+ combine pass when splits > 1)
+    _after(dev)
+    return out, lse

@@ -1,0 +1,130 @@
+"""Drop-in for serving_engine/paged_attention_kernel.py on B200.
+
+Same public names, signatures and return values as the reference module:
+
+* ``paged_flash_attention(q, k_cache, v_cache, metadata, num_q_heads,
+  num_kv_heads, scale, is_causal=True) -> (o, l)``
+  (paged_attention_kernel.py:125-160), and
+* ``build_paged_batch_metadata(scheduler_output, device="cuda") -> dict``
+  (paged_attention_kernel.py:163-200),
+
+but the attention runs in the sm_100a library (no Triton, no CPU path). The
+metadata dict keeps every key the reference returns and adds a few host-known
+values (``max_q_len``, per-token rows, ...) so the launcher never has to read a
+device tensor back: the reference's per-layer ``q_lens.max().item()`` sync
+(paged_attention_kernel.py:133) is gone. A metadata dict built elsewhere (e.g.
+by the reference's own builder) is accepted too; rows are then located on the
+device by binary search over q_starts.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import ops
+
+PAGED_K_TILE_SIZE = ops.BLOCK_SIZE  # one physical block per key tile (paged_attention_kernel.py:12)
+PAGED_Q_TILE_SIZE = 16
+
+
+def _is_prefill(req) -> bool:
+    # RequestPhase.NEEDS_PREFILL of serving_engine/request.py:9-18, compared by
+    # name so this module does not import the engine package.
+    phase = req.phase
+    return getattr(phase, "name", phase) == "NEEDS_PREFILL"
+
+
+def build_paged_batch_metadata(scheduler_output, device="cuda") -> dict:
+    """Per-step metadata, reused by every layer of the step.
+
+    Row semantics follow paged_attention_kernel.py:171-187: a prefill row gets
+    q_len = its chunk, k_len = num_computed_tokens + chunk, q_pos_offset =
+    num_computed_tokens; a decode row gets q_len = 1, k_len = total_len,
+    q_pos_offset = total_len - 1. Block tables are zero-padded to the widest row.
+    All int32 arrays travel in ONE host-to-device copy from pinned memory.
+    """
+    q_lens, k_lens, q_starts, q_pos_offsets, tables = [], [], [], [], []
+    start = 0
+    for req in scheduler_output.scheduled_requests:
+        if _is_prefill(req):
+            nq = scheduler_output.prefill_chunk_sizes[req.request_id]
+            nk = req.num_computed_tokens + nq
+            qp = req.num_computed_tokens
+        else:
+            nq = 1
+            nk = req.total_len
+            qp = req.total_len - 1
+        q_lens.append(nq)
+        k_lens.append(nk)
+        q_starts.append(start)
+        q_pos_offsets.append(qp)
+        tables.append(req.block_table)
+        start += nq
+    return metadata_from_lists(q_lens, k_lens, q_starts, q_pos_offsets, tables, device)
+
+
+def metadata_from_lists(q_lens, k_lens, q_starts, q_pos_offsets, tables, device="cuda") -> dict:
+    rows = len(q_lens)
+    total_query = sum(q_lens)
+    width = max((len(bt) for bt in tables), default=0)
+    item_row = []
+    for r, n in enumerate(q_lens):
+        item_row.extend([r] * n)
+    packed = list(q_lens) + list(k_lens) + list(q_starts) + list(q_pos_offsets)
+    for bt in tables:
+        packed.extend(bt)
+        packed.extend([0] * (width - len(bt)))
+    packed.extend(item_row)
+    host = torch.tensor(packed, dtype=torch.int32)
+    dev = torch.device(device)
+    if dev.type == "cuda":
+        buf = host.pin_memory().to(dev, non_blocking=True)
+    else:
+        buf = host.to(dev)
+    o = 0
+    views = []
+    for n in (rows, rows, rows, rows):
+        views.append(buf[o:o + n])
+        o += n
+    block_table = buf[o:o + rows * width].view(rows, width)
+    o += rows * width
+    item_row_t = buf[o:o + total_query]
+    max_block_id = max((max(bt) for bt in tables if len(bt)), default=-1)
+    return {
+        "q_lens": views[0],
+        "k_lens": views[1],
+        "q_starts": views[2],
+        "q_pos_offsets": views[3],
+        "block_table": block_table,
+        "block_table_row_stride": width,
+        "total_query": total_query,
+        # host-known extras (not in the reference's dict)
+        "max_q_len": max(q_lens, default=0),
+        "item_row": item_row_t,
+        "max_block_id": max_block_id,
+        "max_k_len": max(k_lens, default=0),
+    }
+
+
+def paged_flash_attention(q, k_cache, v_cache, metadata, num_q_heads, num_kv_heads, scale, is_causal=True):
+    """Paged attention over one layer's block-structured pool.
+
+    q: [total_query, num_q_heads, head_dim]; k_cache/v_cache: [num_blocks,
+    block_size, num_kv_heads, head_dim] (not pre-gathered); metadata as built by
+    build_paged_batch_metadata. Returns (o like q, l fp32 [total_query,
+    num_q_heads]) where l is the log-sum-exp of the scaled scores (natural log).
+    """
+    rows = metadata["q_lens"].shape[0]
+    width = int(metadata["block_table_row_stride"])
+    mbid = metadata.get("max_block_id")
+    if mbid is not None and mbid >= k_cache.shape[0]:
+        raise ValueError(f"paged_flash_attention: block id {mbid} outside the pool of {k_cache.shape[0]} blocks")
+    mk = metadata.get("max_k_len")
+    if mk is not None and mk > width * ops.BLOCK_SIZE:
+        raise ValueError(f"paged_flash_attention: k_len {mk} exceeds the block table width {width} x {ops.BLOCK_SIZE}")
+    o = torch.empty_like(q)
+    lse = torch.empty((q.shape[0], num_q_heads), dtype=torch.float32, device=q.device)
+    if rows == 0 or q.shape[0] == 0:
+        return o, lse
+    return ops.paged_decode(q, k_cache, v_cache, metadata["block_table"], metadata["q_starts"], metadata["k_lens"],
+                            metadata["q_pos_offsets"], num_q_heads, num_kv_heads, scale, is_causal,
+                            item_row=metadata.get("item_row"), out=o, lse=lse)

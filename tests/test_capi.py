@@ -1,0 +1,111 @@
+"""The C-ABI library loads, exports every symbol the header declares, and its
+host-side argument checks reject bad calls before touching the GPU."""
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+from serving_engine_b200 import _lib
+from serving_engine_b200.build import LIB_PATH, build
+
+HEADER = Path(__file__).resolve().parent.parent / "include" / "serving_engine_b200.h"
+
+
+@pytest.fixture(scope="module")
+def lib():
+    build()
+    return _lib.lib()
+
+
+def declared_functions():
+    text = HEADER.read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(seb_\w+)\s*\(", text)))
+
+
+def test_header_declares_entry_points():
+    names = declared_functions()
+    for n in ("seb_kv_append", "seb_copy_blocks", "seb_paged_decode", "seb_paged_decode_workspace_size",
+              "seb_last_error", "seb_version", "seb_status_string"):
+        assert n in names
+
+
+def test_library_exports_every_declared_symbol(lib):
+    assert LIB_PATH.exists()
+    for name in declared_functions():
+        assert hasattr(lib, name), name
+        assert name in _lib.SIGNATURES, f"{name} has no ctypes signature"
+
+
+def test_only_c_abi_symbols_are_exported(lib):
+    """Every seb_* symbol the library exports is declared in the header."""
+    import subprocess
+
+    out = subprocess.run(["nm", "-D", "--defined-only", str(LIB_PATH)], capture_output=True, text=True).stdout
+    exported = {line.split()[-1] for line in out.splitlines() if " T " in line and "seb_" in line}
+    assert exported <= set(declared_functions()), exported - set(declared_functions())
+
+
+def test_version_and_status_strings(lib):
+    assert b"sm_100a" in lib.seb_version()
+    assert lib.seb_status_string(_lib.SEB_EINVAL) == b"invalid argument"
+    assert lib.seb_status_string(_lib.SEB_EWORKSPACE) == b"workspace too small"
+
+
+def test_kv_append_rejects_bad_dtype_without_gpu(lib):
+    st = lib.seb_kv_append(1024, 64, 64, 1024, 64, 64, 4, 2048, 4096, 8192, 8, 1, 64, 99, None, None)
+    assert st == _lib.SEB_EINVAL
+    assert b"dtype" in lib.seb_last_error()
+
+
+def test_kv_append_zero_tokens_is_noop(lib):
+    assert lib.seb_kv_append(None, 0, 0, None, 0, 0, 0, None, None, None, 8, 1, 64, _lib.SEB_BF16, None, None) == 0
+
+
+def test_kv_append_rejects_null(lib):
+    st = lib.seb_kv_append(None, 64, 64, None, 64, 64, 4, None, None, None, 8, 1, 64, _lib.SEB_BF16, None, None)
+    assert st == _lib.SEB_EINVAL and b"NULL" in lib.seb_last_error()
+
+
+def test_copy_blocks_validation(lib):
+    assert lib.seb_copy_blocks(None, 2, 0, 8, 4096, None, None, 0, None, None) == 0
+    assert lib.seb_copy_blocks(None, 2, 0, 8, 4096, None, None, 3, None, None) == _lib.SEB_EINVAL
+
+
+def _decode_args(**over):
+    a = dict(q=4096, qs=4096, qh=128, kc=1 << 20, vc=1 << 21, nb=64, bt=8192, bts=8, mb=8, qst=9000, kl=9100,
+             qp=9200, rows=2, tq=2, iq=None, ir=None, items=2, hq=32, hkv=8, d=128, dtype=_lib.SEB_BF16,
+             scale=0.088, causal=1, bps=0, out=1 << 22, os=4096, oh=128, lse=1 << 23, ls=32, ws=None, wsb=0,
+             err=None, stream=None)
+    a.update(over)
+    return list(a.values())
+
+
+def test_paged_decode_validation(lib):
+    assert lib.seb_paged_decode(*_decode_args(items=0)) == 0
+    assert lib.seb_paged_decode(*_decode_args(hq=30)) == _lib.SEB_EINVAL
+    assert b"multiple" in lib.seb_last_error()
+    assert lib.seb_paged_decode(*_decode_args(hq=64, hkv=2)) == _lib.SEB_EINVAL  # group 32 > 16
+    assert lib.seb_paged_decode(*_decode_args(kc=(1 << 20) + 8)) == _lib.SEB_EINVAL  # misaligned pool
+    assert lib.seb_paged_decode(*_decode_args(bts=4)) == _lib.SEB_EINVAL  # stride < max_blocks
+    assert lib.seb_paged_decode(*_decode_args(dtype=7)) == _lib.SEB_EINVAL
+    # split-K needed (max_blocks 512) but no workspace
+    assert lib.seb_paged_decode(*_decode_args(mb=512, bts=512)) == _lib.SEB_EWORKSPACE
+
+
+def test_decode_workspace_size(lib):
+    assert lib.seb_paged_decode_workspace_size(0, 32, 8, 128, 512, 0) == 0
+    # one split per item -> no workspace
+    assert lib.seb_paged_decode_workspace_size(64, 32, 8, 128, 8, 8) == 0
+    n = lib.seb_paged_decode_workspace_size(64, 32, 8, 128, 512, 32)
+    assert n == 64 * 32 * 16 * (128 + 2) * 4
+
+
+def test_ctypes_signatures_match_header_arity():
+    text = re.sub(r"/\*.*?\*/", "", HEADER.read_text(), flags=re.S)
+    for name, (_, args) in _lib.SIGNATURES.items():
+        m = re.search(rf"\b{name}\s*\(([^;]*)\)\s*;", text)
+        assert m, name
+        params = [p for p in m.group(1).split(",") if p.strip() and p.strip() != "void"]
+        assert len(params) == len(args), (name, len(params), len(args))
