@@ -55,6 +55,7 @@ def parse_args():
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--batch", type=int, default=64)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer e2e leg (short profiling runs)")
     return ap.parse_args()
 
 
@@ -173,7 +174,7 @@ def run_ours(args, rank, world, device, dist):
     ops.check_device_errors(device)
 
     # ---- e2e through the public API with host buffers
-    e2e = run_e2e(args, b, device, dist, world)
+    e2e = None if args.no_e2e else run_e2e(args, b, device, dist, world)
 
     result = {
         "metric": METRIC,

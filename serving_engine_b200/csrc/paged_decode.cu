@@ -322,12 +322,20 @@ __global__ void __launch_bounds__(WARPS * 32) decode_mma_kernel(const DecodePara
         oacc[mt][nt][3] *= corr[nt][1];
       }
 
-    // P^T (k = keys, n = heads) operand fragments.
-    uint32_t pb0[NTH], pb1[NTH];
+    // P^T (k = keys, n = heads) operand fragments. P is split into a 16-bit
+    // high part and the 16-bit rounding of its remainder, so P V is exact to
+    // ~2^-17 relative instead of carrying the 2^-9 error of one bf16 rounding.
+    uint32_t pb0[NTH], pb1[NTH], pl0[NTH], pl1[NTH];
 #pragma unroll
     for (int nt = 0; nt < NTH; ++nt) {
-      pb0[nt] = movmatrix_trans(Mma<T>::pack(sacc[nt][0], sacc[nt][1]));
-      pb1[nt] = movmatrix_trans(Mma<T>::pack(sacc[nt][2], sacc[nt][3]));
+      const uint32_t h0 = Mma<T>::pack(sacc[nt][0], sacc[nt][1]);
+      const uint32_t h1 = Mma<T>::pack(sacc[nt][2], sacc[nt][3]);
+      const float2 f0 = Mma<T>::unpack(h0);
+      const float2 f1 = Mma<T>::unpack(h1);
+      pb0[nt] = movmatrix_trans(h0);
+      pb1[nt] = movmatrix_trans(h1);
+      pl0[nt] = movmatrix_trans(Mma<T>::pack(sacc[nt][0] - f0.x, sacc[nt][1] - f0.y));
+      pl1[nt] = movmatrix_trans(Mma<T>::pack(sacc[nt][2] - f1.x, sacc[nt][3] - f1.y));
     }
 
     // O^T += V^T P^T : head_dim x heads.
@@ -338,7 +346,10 @@ __global__ void __launch_bounds__(WARPS * 32) decode_mma_kernel(const DecodePara
       uint32_t a0, a1, a2, a3;
       ldmatrix_x4_trans(vaddr + mt * 32, a0, a1, a2, a3);
 #pragma unroll
-      for (int nt = 0; nt < NTH; ++nt) Mma<T>::run(oacc[mt][nt], a0, a1, a2, a3, pb0[nt], pb1[nt]);
+      for (int nt = 0; nt < NTH; ++nt) {
+        Mma<T>::run(oacc[mt][nt], a0, a1, a2, a3, pb0[nt], pb1[nt]);
+        Mma<T>::run(oacc[mt][nt], a0, a1, a2, a3, pl0[nt], pl1[nt]);
+      }
     }
     __syncwarp();
     if (j + STAGES < nb) {
