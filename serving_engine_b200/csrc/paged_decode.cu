@@ -24,8 +24,10 @@
 // Roofline: HBM. Algorithmic bytes = sum_items k_len * num_kv_heads * head_dim *
 // 2 (K and V) * elem; each KV byte is read once regardless of the group size.
 #include "seb_common.cuh"
+#include "seb_tma.cuh"
 
 #include <cmath>
+#include <type_traits>
 
 namespace seb {
 namespace {
@@ -144,24 +146,31 @@ __device__ __forceinline__ int load_block_ids(const DecodeParams& p, const ItemI
 // --------------------------------------------------------------------------
 // Tensor-core path (fp16 / bf16).
 // --------------------------------------------------------------------------
+// Shared-memory tile of one 16-token block and one kv head: head_dim/64 panels
+// of 16 rows x 128 bytes, written by TMA with 128-byte swizzling (16-byte chunk
+// c of row r lands at chunk c ^ (r & 7)), so every ldmatrix phase (8 rows, one
+// logical chunk) touches 8 distinct bank groups.
 template <int D>
-struct MmaTile {
-  static constexpr int kRowBytes = D * 2;
-  static constexpr int kPitch = kRowBytes + 16;  // 16-byte skew: conflict-free ldmatrix
-  static constexpr int kTile = 16 * kPitch;      // one 16-row K or V tile
-  static constexpr int kStage = 2 * kTile;
+struct TmaTile {
+  static constexpr int kPanels = D / 64;
+  static constexpr int kPanel = 16 * 128;
+  static constexpr int kTile = kPanels * kPanel;  // K or V
+  static constexpr int kStage = 2 * kTile;        // K then V
 };
 
-template <int WARPS, int STAGES>
-constexpr int bar_bytes() {
-  return ((WARPS * STAGES * 8 + 127) / 128) * 128;
-}
+constexpr int kBarRegion = 1024;  // mbarriers, then the 1 KB-aligned rings
+
+// Threshold (log2 units) by which a block maximum must exceed the running
+// reference maximum before O and l are rescaled: probabilities stay <= 2^8.
+constexpr float kRescaleThreshold = 8.0f;
 
 template <typename T, int D, int NTH, int STAGES, int WARPS>
-__global__ void __launch_bounds__(WARPS * 32) decode_mma_kernel(const DecodeParams p) {
-  using Tile = MmaTile<D>;
+__global__ void __launch_bounds__(WARPS * 32)
+    decode_mma_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap tmap_k,
+                      const __grid_constant__ CUtensorMap tmap_v) {
+  using Tile = TmaTile<D>;
   constexpr int KS = D / 16;
-  extern __shared__ __align__(128) char smem[];
+  extern __shared__ __align__(1024) char smem_raw[];
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int g = lane >> 2;
@@ -199,51 +208,46 @@ __global__ void __launch_bounds__(WARPS * 32) decode_mma_kernel(const DecodePara
     }
   }
 
-  char* ring = smem + bar_bytes<WARPS, STAGES>() + warp * STAGES * Tile::kStage;
-  const uint32_t bar0 = smem_u32(smem) + warp * STAGES * 8;
+  // 1 KB-aligned layout: [mbarriers (1 KB)] [warp 0 ring] [warp 1 ring] ...
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;
+  const uint32_t bar0 = base + warp * STAGES * 8;
+  const uint32_t ring = base + kBarRegion + warp * STAGES * Tile::kStage;
+  char* ring_ptr = smem_raw + (ring - raw);
   if (lane == 0) {
 #pragma unroll
     for (int s = 0; s < STAGES; ++s) mbar_init(bar0 + 8 * s, 1);
     fence_mbar_init();
+    prefetch_tensor_map(&tmap_k);
+    prefetch_tensor_map(&tmap_v);
   }
   __syncwarp();
 
-  const char* kc = p.k_cache;
-  const char* vc = p.v_cache;
-  // Stage block j (relative to b0) into ring slot j % STAGES.
+  // Stage block j (relative to b0) into ring slot j % STAGES (lane 0 issues).
   auto issue = [&](int j) {
-    const int s = j % STAGES;
-    const int blk = b0 + j;
     const int bid = __shfl_sync(kFull, bid_reg, j);
-    const int vis = min(16, it.n_vis - blk * 16);
-    const int real = min(vis, it.k_len - blk * 16);
-    const int ncopy = bid >= 0 ? real : 0;
-    char* st = ring + s * Tile::kStage;
-    fence_proxy_async_smem();
-    __syncwarp();
-    if (lane == 0) mbar_arrive_expect_tx(bar0 + 8 * s, (uint32_t)(ncopy * 2 * Tile::kRowBytes));
-    __syncwarp();
-    const int r = lane & 15;
-    const int isv = lane >> 4;
-    char* dst = st + isv * Tile::kTile + r * Tile::kPitch;
-    if (r < ncopy) {
-      const char* src = (isv ? vc : kc) +
-                        (((int64_t)bid * 16 + r) * p.hkv + kvh) * (int64_t)Tile::kRowBytes;
-      bulk_g2s(smem_u32(dst), src, Tile::kRowBytes, bar0 + 8 * s);
-    } else if (isv) {
-      // Zero V rows of keys that are padding or unreadable, so P = 0 (masked) or
-      // P = exp(-m) (phantom key, score 0) multiplies exact zeros.
+    if (lane == 0) {
+      const int s = j % STAGES;
+      const uint32_t bar = bar0 + 8 * s;
+      const uint32_t dk = ring + s * Tile::kStage;
+      if (bid >= 0) {
+        mbar_arrive_expect_tx(bar, Tile::kStage);
 #pragma unroll
-      for (int c = 0; c < Tile::kRowBytes; c += 16)
-        *reinterpret_cast<uint4*>(dst + c) = make_uint4(0u, 0u, 0u, 0u);
+        for (int pn = 0; pn < Tile::kPanels; ++pn) {
+          tma_load_3d(dk + pn * Tile::kPanel, &tmap_k, pn * 64, kvh, bid * 16, bar);
+          tma_load_3d(dk + Tile::kTile + pn * Tile::kPanel, &tmap_v, pn * 64, kvh, bid * 16, bar);
+        }
+      } else {
+        mbar_arrive_expect_tx(bar, 0);
+      }
     }
   };
 
-  float m_run[NTH][2], l_part[NTH][2];
+  float m_ref[NTH][2], l_part[NTH][2];
   float oacc[KS][NTH][4];
 #pragma unroll
   for (int nt = 0; nt < NTH; ++nt) {
-    m_run[nt][0] = m_run[nt][1] = -INFINITY;
+    m_ref[nt][0] = m_ref[nt][1] = -INFINITY;
     l_part[nt][0] = l_part[nt][1] = 0.f;
 #pragma unroll
     for (int mt = 0; mt < KS; ++mt) oacc[mt][nt][0] = oacc[mt][nt][1] = oacc[mt][nt][2] = oacc[mt][nt][3] = 0.f;
@@ -251,75 +255,128 @@ __global__ void __launch_bounds__(WARPS * 32) decode_mma_kernel(const DecodePara
 
   const int npro = min(STAGES, max(nb, 0));
   for (int j = 0; j < npro; ++j) issue(j);
-  __syncwarp();
+
+  // Per-lane swizzled offsets. K (ldmatrix, A = keys x dims): row = lane & 15,
+  // logical chunk 2*ks + (lane >> 4). V (ldmatrix.trans, A = dims x keys):
+  // row = (lane & 7) + 8 * (lane >> 4), logical chunk 2*mt + ((lane >> 3) & 1).
+  // Chunk c of a panel row r sits at physical chunk (c & 7) ^ (r & 7).
+  const int krow = lane & 15;
+  const int khi = lane >> 4;
+  const int vrow = (lane & 7) + 8 * (lane >> 4);
+  const int vhi = (lane >> 3) & 1;
+  uint32_t koff[4], voff[4];
+#pragma unroll
+  for (int m = 0; m < 4; ++m) {
+    koff[m] = krow * 128 + ((((2 * m) | khi) ^ (krow & 7)) << 4);
+    voff[m] = vrow * 128 + ((((2 * m) | vhi) ^ (vrow & 7)) << 4);
+  }
 
   bool timed_out = false;
   for (int j = 0; j < nb; ++j) {
     const int s = j % STAGES;
     if (!mbar_wait_bounded(bar0 + 8 * s, (uint32_t)((j / STAGES) & 1))) {
       timed_out = true;
-      // Drain the copies still in flight (bounded) before leaving the CTA.
       for (int jj = j + 1; jj < min(j + STAGES, nb); ++jj)
         mbar_wait_bounded(bar0 + 8 * (jj % STAGES), (uint32_t)((jj / STAGES) & 1), 1u << 16);
       break;
     }
-    const char* sk = ring + s * Tile::kStage;
-    const char* sv = sk + Tile::kTile;
+    const uint32_t sk = ring + s * Tile::kStage;
+    const uint32_t sv = sk + Tile::kTile;
+    const int blk = b0 + j;
+    const bool bad = __shfl_sync(kFull, bid_reg, j) < 0;
+    const int real = bad ? 0 : min(16, it.k_len - blk * 16);
+    if (real < 16) {
+      // V rows of zero-padded or unreadable keys must be exact zeros: the pool
+      // past k_len (or an unreadable block) may hold anything, even NaN.
+      char* vrows = ring_ptr + (sv - ring);
+      for (int c = lane; c < (16 - real) * Tile::kPanels * 8; c += 32) {
+        const int row = real + c / (Tile::kPanels * 8);
+        const int rem = c % (Tile::kPanels * 8);
+        *reinterpret_cast<uint4*>(vrows + (rem >> 3) * Tile::kPanel + row * 128 + (rem & 7) * 16) =
+            make_uint4(0u, 0u, 0u, 0u);
+      }
+      fence_proxy_async_smem();  // order these writes before TMA refills the slot
+      __syncwarp();
+    }
 
-    // S^T = K Q^T : 16 keys x (8*NTH) heads, fp32 accumulate.
-    float sacc[NTH][4];
+    // S^T = K Q^T : 16 keys x (8*NTH) heads; two accumulation chains for ILP.
+    float sa[NTH][4], sb[NTH][4];
 #pragma unroll
-    for (int nt = 0; nt < NTH; ++nt) sacc[nt][0] = sacc[nt][1] = sacc[nt][2] = sacc[nt][3] = 0.f;
-    const uint32_t kaddr = smem_u32(sk + (lane & 15) * Tile::kPitch + (lane >> 4) * 16);
+    for (int nt = 0; nt < NTH; ++nt)
+#pragma unroll
+      for (int c = 0; c < 4; ++c) sa[nt][c] = sb[nt][c] = 0.f;
 #pragma unroll
     for (int ks = 0; ks < KS; ++ks) {
       uint32_t a0, a1, a2, a3;
-      ldmatrix_x4(kaddr + ks * 32, a0, a1, a2, a3);
+      ldmatrix_x4(sk + (ks >> 2) * Tile::kPanel + koff[ks & 3], a0, a1, a2, a3);
 #pragma unroll
-      for (int nt = 0; nt < NTH; ++nt) Mma<T>::run(sacc[nt], a0, a1, a2, a3, qf[ks][nt][0], qf[ks][nt][1]);
+      for (int nt = 0; nt < NTH; ++nt) {
+        if (ks & 1) Mma<T>::run(sb[nt], a0, a1, a2, a3, qf[ks][nt][0], qf[ks][nt][1]);
+        else Mma<T>::run(sa[nt], a0, a1, a2, a3, qf[ks][nt][0], qf[ks][nt][1]);
+      }
     }
 
-    // Scale into the log2 domain, mask, online softmax per head column. A block
-    // whose id was out of range was not copied: all of its keys are masked.
-    const bool bad = __shfl_sync(kFull, bid_reg, j) < 0;
-    const int key0 = (b0 + j) * 16 + g;
-    float corr[NTH][2];
+    // Scale into the log2 domain and mask (keys past the visible range: -inf;
+    // zero-padded keys of the last block inside it: score 0).
+    const int key0 = blk * 16 + g;
+    float x[NTH][4];
 #pragma unroll
-    for (int nt = 0; nt < NTH; ++nt) {
+    for (int nt = 0; nt < NTH; ++nt)
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         const int key = key0 + (c >> 1) * 8;
-        float x = sacc[nt][c] * p.scale_log2;
-        if (bad || key >= it.n_vis) x = -INFINITY;
-        else if (key >= it.k_len) x = 0.f;  // zero-padded key of the last block
-        sacc[nt][c] = x;
+        float v = (sa[nt][c] + sb[nt][c]) * p.scale_log2;
+        if (bad || key >= it.n_vis) v = -INFINITY;
+        else if (key >= it.k_len) v = 0.f;
+        x[nt][c] = v;
       }
+
+    // Online softmax per head column with a lazily updated reference max.
+    float mb[NTH][2];
+    bool need = false;
+#pragma unroll
+    for (int nt = 0; nt < NTH; ++nt)
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
-        float mb = fmaxf(sacc[nt][h], sacc[nt][h + 2]);
-        mb = fmaxf(mb, __shfl_xor_sync(kFull, mb, 4));
-        mb = fmaxf(mb, __shfl_xor_sync(kFull, mb, 8));
-        mb = fmaxf(mb, __shfl_xor_sync(kFull, mb, 16));
-        const float m_new = fmaxf(m_run[nt][h], mb);
-        const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
-        const float cr = exp2f(m_run[nt][h] - m_use);
-        const float p0 = exp2f(sacc[nt][h] - m_use);
-        const float p1 = exp2f(sacc[nt][h + 2] - m_use);
-        l_part[nt][h] = l_part[nt][h] * cr + p0 + p1;
-        m_run[nt][h] = m_new;
-        corr[nt][h] = cr;
-        sacc[nt][h] = p0;
-        sacc[nt][h + 2] = p1;
+        float v = fmaxf(x[nt][h], x[nt][h + 2]);
+        v = fmaxf(v, __shfl_xor_sync(kFull, v, 4));
+        v = fmaxf(v, __shfl_xor_sync(kFull, v, 8));
+        v = fmaxf(v, __shfl_xor_sync(kFull, v, 16));
+        mb[nt][h] = v;
+        need |= v > m_ref[nt][h] + kRescaleThreshold;
       }
+    if (__any_sync(kFull, need)) {
+      float corr[NTH][2];
+#pragma unroll
+      for (int nt = 0; nt < NTH; ++nt)
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          if (mb[nt][h] > m_ref[nt][h] + kRescaleThreshold) {
+            corr[nt][h] = exp2f(m_ref[nt][h] - mb[nt][h]);  // 0 when m_ref is -inf
+            m_ref[nt][h] = mb[nt][h];
+          } else {
+            corr[nt][h] = 1.f;
+          }
+          l_part[nt][h] *= corr[nt][h];
+        }
+#pragma unroll
+      for (int mt = 0; mt < KS; ++mt)
+#pragma unroll
+        for (int nt = 0; nt < NTH; ++nt) {
+          oacc[mt][nt][0] *= corr[nt][0];
+          oacc[mt][nt][1] *= corr[nt][1];
+          oacc[mt][nt][2] *= corr[nt][0];
+          oacc[mt][nt][3] *= corr[nt][1];
+        }
     }
 #pragma unroll
-    for (int mt = 0; mt < KS; ++mt)
+    for (int nt = 0; nt < NTH; ++nt)
 #pragma unroll
-      for (int nt = 0; nt < NTH; ++nt) {
-        oacc[mt][nt][0] *= corr[nt][0];
-        oacc[mt][nt][1] *= corr[nt][1];
-        oacc[mt][nt][2] *= corr[nt][0];
-        oacc[mt][nt][3] *= corr[nt][1];
+      for (int h = 0; h < 2; ++h) {
+        const float m_use = m_ref[nt][h] == -INFINITY ? 0.f : m_ref[nt][h];
+        x[nt][h] = exp2f(x[nt][h] - m_use);
+        x[nt][h + 2] = exp2f(x[nt][h + 2] - m_use);
+        l_part[nt][h] += x[nt][h] + x[nt][h + 2];
       }
 
     // P^T (k = keys, n = heads) operand fragments. P is split into a 16-bit
@@ -328,23 +385,21 @@ __global__ void __launch_bounds__(WARPS * 32) decode_mma_kernel(const DecodePara
     uint32_t pb0[NTH], pb1[NTH], pl0[NTH], pl1[NTH];
 #pragma unroll
     for (int nt = 0; nt < NTH; ++nt) {
-      const uint32_t h0 = Mma<T>::pack(sacc[nt][0], sacc[nt][1]);
-      const uint32_t h1 = Mma<T>::pack(sacc[nt][2], sacc[nt][3]);
+      const uint32_t h0 = Mma<T>::pack(x[nt][0], x[nt][1]);
+      const uint32_t h1 = Mma<T>::pack(x[nt][2], x[nt][3]);
       const float2 f0 = Mma<T>::unpack(h0);
       const float2 f1 = Mma<T>::unpack(h1);
       pb0[nt] = movmatrix_trans(h0);
       pb1[nt] = movmatrix_trans(h1);
-      pl0[nt] = movmatrix_trans(Mma<T>::pack(sacc[nt][0] - f0.x, sacc[nt][1] - f0.y));
-      pl1[nt] = movmatrix_trans(Mma<T>::pack(sacc[nt][2] - f1.x, sacc[nt][3] - f1.y));
+      pl0[nt] = movmatrix_trans(Mma<T>::pack(x[nt][0] - f0.x, x[nt][1] - f0.y));
+      pl1[nt] = movmatrix_trans(Mma<T>::pack(x[nt][2] - f1.x, x[nt][3] - f1.y));
     }
 
     // O^T += V^T P^T : head_dim x heads.
-    const uint32_t vaddr =
-        smem_u32(sv + ((lane & 7) + (lane >> 4) * 8) * Tile::kPitch + ((lane >> 3) & 1) * 16);
 #pragma unroll
     for (int mt = 0; mt < KS; ++mt) {
       uint32_t a0, a1, a2, a3;
-      ldmatrix_x4_trans(vaddr + mt * 32, a0, a1, a2, a3);
+      ldmatrix_x4_trans(sv + (mt >> 2) * Tile::kPanel + voff[mt & 3], a0, a1, a2, a3);
 #pragma unroll
       for (int nt = 0; nt < NTH; ++nt) {
         Mma<T>::run(oacc[mt][nt], a0, a1, a2, a3, pb0[nt], pb1[nt]);
@@ -352,10 +407,7 @@ __global__ void __launch_bounds__(WARPS * 32) decode_mma_kernel(const DecodePara
       }
     }
     __syncwarp();
-    if (j + STAGES < nb) {
-      issue(j + STAGES);
-      __syncwarp();
-    }
+    if (j + STAGES < nb) issue(j + STAGES);
   }
   if (timed_out) {
     if (lane == 0) atomic_or_err(p.err, SEB_ERRBIT_TIMEOUT);
@@ -389,7 +441,7 @@ __global__ void __launch_bounds__(WARPS * 32) decode_mma_kernel(const DecodePara
           op[mt * 16 + g] = Elem<T>::from_float(oacc[mt][nt][h] / l_tot[nt][h]);
           op[mt * 16 + g + 8] = Elem<T>::from_float(oacc[mt][nt][h + 2] / l_tot[nt][h]);
         }
-        if (g == 0) p.lse[(int64_t)it.qtok * p.lse_st + qh] = m_run[nt][h] * kLn2 + logf(l_tot[nt][h]);
+        if (g == 0) p.lse[(int64_t)it.qtok * p.lse_st + qh] = m_ref[nt][h] * kLn2 + logf(l_tot[nt][h]);
       }
   } else {
 #pragma unroll
@@ -407,7 +459,7 @@ __global__ void __launch_bounds__(WARPS * 32) decode_mma_kernel(const DecodePara
           wo[mt * 16 + g + 8] = oacc[mt][nt][h + 2];
         }
         if (g == 0) {
-          p.ws_ml[slot * 2] = m_run[nt][h];
+          p.ws_ml[slot * 2] = m_ref[nt][h];
           p.ws_ml[slot * 2 + 1] = l_tot[nt][h];
         }
       }
@@ -528,10 +580,13 @@ __global__ void __launch_bounds__(WARPS * 32) decode_simt_kernel(const DecodePar
 }
 
 // --------------------------------------------------------------------------
-// Combine pass: one warp per (item, q head) with >= 2 splits.
+// Combine pass: one warp per (item, q head) with >= 2 splits. Lane s first
+// turns split s's (m, l) into its weight 2^(m_s - M); then each lane owns D/32
+// consecutive head dims and sums the weighted partial O of every split.
 // --------------------------------------------------------------------------
 template <typename T, int D>
 __global__ void __launch_bounds__(128) decode_combine_kernel(const DecodeParams p) {
+  constexpr int VPL = D / 32;  // values per lane (2, 4 or 8)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int64_t w = (int64_t)blockIdx.x * 4 + warp;
@@ -542,30 +597,72 @@ __global__ void __launch_bounds__(128) decode_combine_kernel(const DecodeParams 
   if (!it.ok || it.n_splits <= 1) return;
   const int64_t base = (item * p.hq + qh) * p.max_splits;
   const float* ml = p.ws_ml + base * 2;
+  const int ns = it.n_splits;
   float mx = -INFINITY;
-  for (int s = lane; s < it.n_splits; s += 32) mx = fmaxf(mx, ml[2 * s]);
+  for (int s = lane; s < ns; s += 32) mx = fmaxf(mx, ml[2 * s]);
 #pragma unroll
   for (int off = 16; off >= 1; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(kFull, mx, off));
   const float m_use = (mx == -INFINITY) ? 0.f : mx;
   float lsum = 0.f;
-  for (int s = lane; s < it.n_splits; s += 32) lsum += ml[2 * s + 1] * exp2f(ml[2 * s] - m_use);
+  for (int s = lane; s < ns; s += 32) lsum += ml[2 * s + 1] * exp2f(ml[2 * s] - m_use);
 #pragma unroll
   for (int off = 16; off >= 1; off >>= 1) lsum += __shfl_xor_sync(kFull, lsum, off);
 
-  T* op = reinterpret_cast<T*>(p.out) + (int64_t)it.qtok * p.o_st + (int64_t)qh * p.o_sh;
-  const float* wo = p.ws_o + base * D;
+  float acc[VPL];
 #pragma unroll
-  for (int i = 0; i < D / 32; ++i) {
-    float acc = 0.f;
-    for (int s = 0; s < it.n_splits; ++s) acc = fmaf(exp2f(ml[2 * s] - m_use), wo[(int64_t)s * D + lane + 32 * i], acc);
-    op[lane + 32 * i] = Elem<T>::from_float(acc / lsum);
+  for (int i = 0; i < VPL; ++i) acc[i] = 0.f;
+  const float* wo = p.ws_o + base * D + lane * VPL;
+  for (int s0 = 0; s0 < ns; s0 += 32) {
+    const int sl = s0 + lane;
+    const float wl = sl < ns ? exp2f(ml[2 * sl] - m_use) : 0.f;
+    const int cnt = min(32, ns - s0);
+#pragma unroll 4
+    for (int k = 0; k < cnt; ++k) {
+      const float wk = __shfl_sync(kFull, wl, k);
+      const float* src = wo + (int64_t)(s0 + k) * D;
+      if constexpr (VPL % 4 == 0) {
+#pragma unroll
+        for (int i = 0; i < VPL; i += 4) {
+          const float4 v = *reinterpret_cast<const float4*>(src + i);
+          acc[i] = fmaf(wk, v.x, acc[i]);
+          acc[i + 1] = fmaf(wk, v.y, acc[i + 1]);
+          acc[i + 2] = fmaf(wk, v.z, acc[i + 2]);
+          acc[i + 3] = fmaf(wk, v.w, acc[i + 3]);
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < VPL; i += 2) {
+          const float2 v = *reinterpret_cast<const float2*>(src + i);
+          acc[i] = fmaf(wk, v.x, acc[i]);
+          acc[i + 1] = fmaf(wk, v.y, acc[i + 1]);
+        }
+      }
+    }
   }
+  T* op = reinterpret_cast<T*>(p.out) + (int64_t)it.qtok * p.o_st + (int64_t)qh * p.o_sh + lane * VPL;
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) op[i] = Elem<T>::from_float(acc[i] / lsum);
   if (lane == 0) p.lse[(int64_t)it.qtok * p.lse_st + qh] = mx * kLn2 + logf(lsum);
 }
 
 // ------------------------------------------------------------------ launching
-constexpr int kMmaWarps = 4;
-constexpr int kMmaStages = 3;
+// Warps per CTA (each its own work item) and ring depth per warp. Shared memory
+// per CTA = 2 KB + warps * stages * 32 * head_dim bytes.
+#ifndef SEB_DECODE_WARPS
+#define SEB_DECODE_WARPS 4
+#endif
+#ifndef SEB_DECODE_STAGES
+#define SEB_DECODE_STAGES 3
+#endif
+constexpr int kMmaWarps = SEB_DECODE_WARPS;
+constexpr int kMmaStages = SEB_DECODE_STAGES;
+template <int D>
+constexpr int mma_stages() {
+  // keep the D = 256 ring within the 227 KB a CTA may use
+  return (kMmaWarps * kMmaStages * TmaTile<D>::kStage + 3 * 1024 <= 227 * 1024)
+             ? kMmaStages
+             : (227 * 1024 - 3 * 1024) / (kMmaWarps * TmaTile<D>::kStage);
+}
 constexpr int kSimtWarps = 4;
 
 int choose_bps(int num_items, int hkv, int64_t max_blocks, int requested) {
@@ -583,8 +680,10 @@ int choose_bps(int num_items, int hkv, int64_t max_blocks, int requested) {
 
 template <typename T, int D, int NTH>
 int launch_mma(const DecodeParams& p, int64_t n_warps, cudaStream_t s) {
-  constexpr int smem = bar_bytes<kMmaWarps, kMmaStages>() + kMmaWarps * kMmaStages * MmaTile<D>::kStage;
-  auto kern = decode_mma_kernel<T, D, NTH, kMmaStages, kMmaWarps>;
+  constexpr int stages = mma_stages<D>();
+  constexpr int smem = 1024 /* alignment slack */ + kBarRegion + kMmaWarps * stages * TmaTile<D>::kStage;
+  static_assert(kMmaWarps * stages * 8 <= kBarRegion, "mbarrier region too small");
+  auto kern = decode_mma_kernel<T, D, NTH, stages, kMmaWarps>;
   static bool attr_set[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -592,8 +691,14 @@ int launch_mma(const DecodeParams& p, int64_t n_warps, cudaStream_t s) {
     SEB_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     attr_set[dev] = true;
   }
+  CUtensorMap tk, tv;
+  const int dtype = std::is_same<T, __nv_bfloat16>::value ? SEB_BF16 : SEB_F16;
+  int rc = kv_tensor_map(&tk, p.k_cache, dtype, p.num_blocks, p.hkv, D);
+  if (rc != SEB_OK) return rc;
+  rc = kv_tensor_map(&tv, p.v_cache, dtype, p.num_blocks, p.hkv, D);
+  if (rc != SEB_OK) return rc;
   const int64_t grid = (n_warps + kMmaWarps - 1) / kMmaWarps;
-  kern<<<(unsigned)grid, kMmaWarps * 32, smem, s>>>(p);
+  kern<<<(unsigned)grid, kMmaWarps * 32, smem, s>>>(p, tk, tv);
   return launch_status("decode_mma_kernel");
 }
 

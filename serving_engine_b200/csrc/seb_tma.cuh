@@ -1,0 +1,34 @@
+// TMA (tensor memory accelerator) helpers: host-side tensor-map creation for the
+// paged KV pool and the device-side tiled bulk-tensor load.
+#pragma once
+
+#include <cuda.h>
+
+#include "seb_common.cuh"
+
+namespace seb {
+
+// Tensor map over one layer's K (or V) pool [num_blocks * 16 rows, num_kv_heads, head_dim]
+// of 16-bit elements, viewed as 3-D (head_dim, num_kv_heads, rows) with a box of
+// (64 elements, 1 head, 16 rows) and 128-byte swizzling: one load brings a 2 KB
+// 16 x 128-byte panel of one block and one kv head into shared memory, laid out
+// as the 128B-swizzled rows ldmatrix reads without bank conflicts.
+// Returns SEB_OK or an SEB_E* status (with seb_last_error set). Results are
+// cached per (pointer, shape), so repeated calls on the same pool cost a lookup.
+int kv_tensor_map(CUtensorMap* out, const void* base, int dtype, int64_t num_blocks, int num_kv_heads,
+                  int head_dim);
+
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map, int x, int y, int z,
+                                            uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, "
+      "%4}], [%5];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(bar)
+      : "memory");
+}
+
+__device__ __forceinline__ void prefetch_tensor_map(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+}  // namespace seb

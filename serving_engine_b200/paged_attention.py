@@ -18,6 +18,9 @@ device by binary search over q_starts.
 """
 from __future__ import annotations
 
+import itertools
+
+import numpy as np
 import torch
 
 from . import ops
@@ -62,47 +65,80 @@ def build_paged_batch_metadata(scheduler_output, device="cuda") -> dict:
     return metadata_from_lists(q_lens, k_lens, q_starts, q_pos_offsets, tables, device)
 
 
+class PackedMetadata:
+    """Host side of one step's metadata: every int32 array in one buffer.
+
+    Layout: q_lens[R] | k_lens[R] | q_starts[R] | q_pos_offsets[R] |
+    block_table[R, W] | item_row[total_query]. ``upload`` issues ONE
+    host-to-device copy (pinned) and returns the metadata dict.
+    """
+
+    def __init__(self, q_lens, k_lens, q_starts, q_pos_offsets, tables):
+        rows = len(q_lens)
+        q_lens_np = np.asarray(q_lens, dtype=np.int32).reshape(rows)
+        lens = np.fromiter((len(t) for t in tables), dtype=np.int64, count=rows)
+        width = int(lens.max()) if rows else 0
+        total_query = int(q_lens_np.sum())
+        o_bt = 4 * rows
+        o_items = o_bt + rows * width
+        packed = torch.zeros(o_items + total_query, dtype=torch.int32)
+        a = packed.numpy()
+        a[0:rows] = q_lens_np
+        a[rows:2 * rows] = k_lens
+        a[2 * rows:3 * rows] = q_starts
+        a[3 * rows:4 * rows] = q_pos_offsets
+        n_ids = int(lens.sum())
+        if n_ids:
+            flat = np.fromiter(itertools.chain.from_iterable(tables), dtype=np.int32, count=n_ids)
+            # destination of id k of row r: o_bt + r * width + k
+            starts = np.repeat(np.arange(rows, dtype=np.int64) * width - np.concatenate(([0], np.cumsum(lens)[:-1])),
+                               lens)
+            a[o_bt + starts + np.arange(n_ids)] = flat
+            self.max_block_id = int(flat.max())
+        else:
+            self.max_block_id = -1
+        a[o_items:] = np.repeat(np.arange(rows, dtype=np.int32), q_lens_np)
+        self.host = packed
+        self.rows, self.width, self.total_query = rows, width, total_query
+        self.max_q_len = int(q_lens_np.max()) if rows else 0
+        self.max_k_len = int(np.max(k_lens)) if rows else 0
+
+    def pin(self) -> "PackedMetadata":
+        if not self.host.is_pinned():
+            self.host = self.host.pin_memory()
+        return self
+
+    @property
+    def nbytes(self) -> int:
+        return self.host.numel() * 4
+
+    def upload(self, device="cuda") -> dict:
+        dev = torch.device(device)
+        if dev.type == "cuda":
+            buf = (self.host if self.host.is_pinned() else self.host.pin_memory()).to(dev, non_blocking=True)
+        else:
+            buf = self.host.clone()
+        rows, width = self.rows, self.width
+        o = 4 * rows
+        return {
+            "q_lens": buf[0:rows],
+            "k_lens": buf[rows:2 * rows],
+            "q_starts": buf[2 * rows:3 * rows],
+            "q_pos_offsets": buf[3 * rows:4 * rows],
+            "block_table": buf[o:o + rows * width].view(rows, width),
+            "block_table_row_stride": width,
+            "total_query": self.total_query,
+            # host-known extras (not in the reference's dict)
+            "max_q_len": self.max_q_len,
+            "item_row": buf[o + rows * width:],
+            "max_block_id": self.max_block_id,
+            "max_k_len": self.max_k_len,
+        }
+
+
 def metadata_from_lists(q_lens, k_lens, q_starts, q_pos_offsets, tables, device="cuda") -> dict:
-    rows = len(q_lens)
-    total_query = sum(q_lens)
-    width = max((len(bt) for bt in tables), default=0)
-    item_row = []
-    for r, n in enumerate(q_lens):
-        item_row.extend([r] * n)
-    packed = list(q_lens) + list(k_lens) + list(q_starts) + list(q_pos_offsets)
-    for bt in tables:
-        packed.extend(bt)
-        packed.extend([0] * (width - len(bt)))
-    packed.extend(item_row)
-    host = torch.tensor(packed, dtype=torch.int32)
-    dev = torch.device(device)
-    if dev.type == "cuda":
-        buf = host.pin_memory().to(dev, non_blocking=True)
-    else:
-        buf = host.to(dev)
-    o = 0
-    views = []
-    for n in (rows, rows, rows, rows):
-        views.append(buf[o:o + n])
-        o += n
-    block_table = buf[o:o + rows * width].view(rows, width)
-    o += rows * width
-    item_row_t = buf[o:o + total_query]
-    max_block_id = max((max(bt) for bt in tables if len(bt)), default=-1)
-    return {
-        "q_lens": views[0],
-        "k_lens": views[1],
-        "q_starts": views[2],
-        "q_pos_offsets": views[3],
-        "block_table": block_table,
-        "block_table_row_stride": width,
-        "total_query": total_query,
-        # host-known extras (not in the reference's dict)
-        "max_q_len": max(q_lens, default=0),
-        "item_row": item_row_t,
-        "max_block_id": max_block_id,
-        "max_k_len": max(k_lens, default=0),
-    }
+    """The metadata dict from per-row host lists (one packed int32 H2D copy)."""
+    return PackedMetadata(q_lens, k_lens, q_starts, q_pos_offsets, tables).upload(device)
 
 
 def paged_flash_attention(q, k_cache, v_cache, metadata, num_q_heads, num_kv_heads, scale, is_causal=True):
