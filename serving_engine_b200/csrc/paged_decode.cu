@@ -652,7 +652,7 @@ __global__ void __launch_bounds__(128) decode_combine_kernel(const DecodeParams 
 #define SEB_DECODE_WARPS 4
 #endif
 #ifndef SEB_DECODE_STAGES
-#define SEB_DECODE_STAGES 3
+#define SEB_DECODE_STAGES 2
 #endif
 constexpr int kMmaWarps = SEB_DECODE_WARPS;
 constexpr int kMmaStages = SEB_DECODE_STAGES;
@@ -667,11 +667,11 @@ constexpr int kSimtWarps = 4;
 
 int choose_bps(int num_items, int hkv, int64_t max_blocks, int requested) {
   if (requested > 0) return requested > kMaxBps ? kMaxBps : requested;
-  // Aim for about four waves of 8 resident warps per SM, assuming rows fill
-  // about half of the block-table width; keep >= 8 blocks so the copy ring
-  // has work to pipeline.
+  // Aim for about two waves of 12 resident warps per SM, assuming rows fill
+  // about half of the block-table width; long splits (up to 32 blocks) keep
+  // the partial-result traffic small, >= 8 blocks keep the copy ring busy.
   const double est_blocks = 0.5 * (double)num_items * hkv * (double)max_blocks;
-  const double slots = (double)num_sms() * 8.0 * 4.0;
+  const double slots = (double)num_sms() * 12.0 * 2.0;
   int bps = (int)std::ceil(est_blocks / slots);
   if (bps < 8) bps = 8;
   if (bps > kMaxBps) bps = kMaxBps;
