@@ -139,6 +139,40 @@ SEB_API int seb_paged_decode(const void* q, int64_t q_stride_token, int64_t q_st
                      int64_t out_stride_head, float* lse, int64_t lse_stride_token,
                      void* workspace, int64_t workspace_bytes, int32_t* err, void* stream);
 
+/*
+ * Allocation-free variant of seb_paged_decode. This entry point has no
+ * counterpart in the reference: it exists for callers that cannot hand the
+ * library a workspace, such as a host runtime whose allocator already owns all
+ * free device memory (the engine sizes its KV pool to most of the free memory
+ * at start-up), or an FFI binding with no access to the framework allocator.
+ *
+ * Arguments and results are those of seb_paged_decode without the workspace.
+ * The split-K scratch is a fixed device array built into the library, of
+ * SEB_NOALLOC_SCRATCH_BYTES (32 MiB), which every GPU that loads the library
+ * holds until the process exits. A call whose scratch need
+ * (seb_paged_decode_workspace_size) exceeds it returns SEB_EWORKSPACE with a
+ * message and launches nothing; callers can raise blocks_per_split or split the
+ * batch. The call itself never calls cudaMalloc or cudaFree.
+ *
+ * The first call on each device looks up the array's device address
+ * (cudaGetSymbolAddress, with that device current) and caches it; make that
+ * first call outside any stream capture. All calls share the one array and
+ * nothing in it needs to start at zero, but calls that overlap on the GPU (for
+ * example on two streams at once) race on it and must be serialised.
+ */
+#define SEB_NOALLOC_SCRATCH_BYTES (32ll << 20)
+
+SEB_API int seb_paged_decode_noalloc(const void* q, int64_t q_stride_token, int64_t q_stride_head,
+                                     const void* k_cache, const void* v_cache, int64_t num_blocks,
+                                     const int32_t* block_table, int64_t block_table_stride,
+                                     int64_t max_blocks, const int32_t* q_starts, const int32_t* k_lens,
+                                     const int32_t* q_pos_offsets, int32_t num_rows, int32_t total_query,
+                                     const int32_t* item_query, const int32_t* item_row, int32_t num_items,
+                                     int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
+                                     int32_t dtype, float scale, int32_t is_causal, int32_t blocks_per_split,
+                                     void* out, int64_t out_stride_token, int64_t out_stride_head,
+                                     float* lse, int64_t lse_stride_token, int32_t* err, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

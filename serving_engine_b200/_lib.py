@@ -55,7 +55,16 @@ SIGNATURES = {
          c_void_p, c_int64,                     # lse, stride
          c_void_p, c_int64, c_void_p, c_void_p],  # workspace, bytes, err, stream
     ),
+    # seb_paged_decode without the workspace pair (built-in scratch)
+    "seb_paged_decode_noalloc": (
+        c_int32,
+        [c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_int64, c_void_p, c_int64, c_int64,
+         c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_void_p, c_void_p, c_int32,
+         c_int32, c_int32, c_int32, c_int32, c_float, c_int32, c_int32,
+         c_void_p, c_int64, c_int64, c_void_p, c_int64, c_void_p, c_void_p],
+    ),
 }
+NOALLOC_SCRATCH_BYTES = 32 << 20  # SEB_NOALLOC_SCRATCH_BYTES
 
 _LIB: ctypes.CDLL | None = None
 

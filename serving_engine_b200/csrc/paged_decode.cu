@@ -27,6 +27,7 @@
 #include "seb_tma.cuh"
 
 #include <cmath>
+#include <mutex>
 #include <type_traits>
 
 namespace seb {
@@ -849,4 +850,79 @@ extern "C" int seb_paged_decode(const void* q, int64_t q_stride_token, int64_t q
     case SEB_F16: return launch_dim<__half>(p, head_dim, n_warps, tc, s);
     default: return launch_dim<float>(p, head_dim, n_warps, false, s);
   }
+}
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant of seb_paged_decode.
+//
+// Its split-K scratch is this file-scope device array, so the call needs no
+// workspace from the caller and performs no device allocation. The array is
+// part of the library image: every GPU that loads the library holds
+// SEB_NOALLOC_SCRATCH_BYTES of it until the process exits. In host code the
+// symbol is only a host-side stand-in, so the device address is looked up with
+// cudaGetSymbolAddress once per device (with that device current) and cached.
+// ---------------------------------------------------------------------------
+static __device__ __align__(256) unsigned char g_noalloc_scratch[SEB_NOALLOC_SCRATCH_BYTES];
+
+namespace seb {
+namespace {
+
+constexpr int kMaxDevices = 64;
+std::mutex g_noalloc_mu;
+void* g_noalloc_addr[kMaxDevices] = {};
+
+// Device address of g_noalloc_scratch on the current device.
+int noalloc_scratch_address(void** out) {
+  int dev = -1;
+  SEB_CHECK_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= kMaxDevices) {
+    set_error("seb_paged_decode_noalloc: device ordinal %d outside [0, %d)", dev, kMaxDevices);
+    return SEB_EINVAL;
+  }
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if (g_noalloc_addr[dev] == nullptr) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess || p == nullptr) {
+      set_error("seb_paged_decode_noalloc: cudaGetSymbolAddress failed on device %d: %s", dev,
+                cudaGetErrorString(e));
+      return SEB_ECUDA;
+    }
+    g_noalloc_addr[dev] = p;
+  }
+  *out = g_noalloc_addr[dev];
+  return SEB_OK;
+}
+
+}  // namespace
+}  // namespace seb
+
+extern "C" int seb_paged_decode_noalloc(const void* q, int64_t q_stride_token, int64_t q_stride_head,
+                                        const void* k_cache, const void* v_cache, int64_t num_blocks,
+                                        const int32_t* block_table, int64_t block_table_stride,
+                                        int64_t max_blocks, const int32_t* q_starts, const int32_t* k_lens,
+                                        const int32_t* q_pos_offsets, int32_t num_rows, int32_t total_query,
+                                        const int32_t* item_query, const int32_t* item_row, int32_t num_items,
+                                        int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
+                                        int32_t dtype, float scale, int32_t is_causal, int32_t blocks_per_split,
+                                        void* out, int64_t out_stride_token, int64_t out_stride_head,
+                                        float* lse, int64_t lse_stride_token, int32_t* err, void* stream) {
+  using namespace seb;
+  clear_error();
+  const int64_t need = seb_paged_decode_workspace_size(num_items, num_q_heads, num_kv_heads, head_dim, max_blocks,
+                                                       blocks_per_split);
+  if (need > (int64_t)SEB_NOALLOC_SCRATCH_BYTES) {
+    set_error("seb_paged_decode_noalloc: this call needs %lld bytes of split-K scratch but the built-in scratch "
+              "holds %lld bytes; use fewer items, more blocks_per_split, or seb_paged_decode with a workspace",
+              (long long)need, (long long)SEB_NOALLOC_SCRATCH_BYTES);
+    return SEB_EWORKSPACE;
+  }
+  void* scratch = nullptr;
+  const int rc = noalloc_scratch_address(&scratch);
+  if (rc != SEB_OK) return rc;
+  return seb_paged_decode(q, q_stride_token, q_stride_head, k_cache, v_cache, num_blocks, block_table,
+                          block_table_stride, max_blocks, q_starts, k_lens, q_pos_offsets, num_rows, total_query,
+                          item_query, item_row, num_items, num_q_heads, num_kv_heads, head_dim, dtype, scale,
+                          is_causal, blocks_per_split, out, out_stride_token, out_stride_head, lse,
+                          lse_stride_token, scratch, (int64_t)SEB_NOALLOC_SCRATCH_BYTES, err, stream);
 }
