@@ -140,6 +140,25 @@ SEB_API int seb_paged_decode(const void* q, int64_t q_stride_token, int64_t q_st
                      void* workspace, int64_t workspace_bytes, int32_t* err, void* stream);
 
 /*
+ * Chunked-prefill paged attention on tcgen05 tensor cores (bf16/fp16, head_dim
+ * 64 or 128, GQA group 1/2/4/8/16): the prefill / mixed use (q_len > 1) of the
+ * reference kernel (paged_attention_kernel.py:16-122), with the semantics stated
+ * above for seb_paged_decode. Computes the rows listed in `rows` (NULL: rows
+ * 0 .. num_prefill_rows-1); `max_q_len` bounds their q_lens and sizes the grid.
+ * q, out: 16-byte aligned, strides multiples of 8 elements. No workspace.
+ */
+SEB_API int seb_paged_prefill(const void* q, int64_t q_stride_token, int64_t q_stride_head,
+                              const void* k_cache, const void* v_cache, int64_t num_blocks,
+                              const int32_t* block_table, int64_t block_table_stride, int64_t max_blocks,
+                              const int32_t* q_starts, const int32_t* q_lens, const int32_t* k_lens,
+                              const int32_t* q_pos_offsets, int32_t num_rows, int32_t total_query,
+                              const int32_t* rows, int32_t num_prefill_rows, int32_t max_q_len,
+                              int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim, int32_t dtype,
+                              float scale, int32_t is_causal, void* out, int64_t out_stride_token,
+                              int64_t out_stride_head, float* lse, int64_t lse_stride_token, int32_t* err,
+                              void* stream);
+
+/*
  * Allocation-free variant of seb_paged_decode. This entry point has no
  * counterpart in the reference: it exists for callers that cannot hand the
  * library a workspace, such as a host runtime whose allocator already owns all

@@ -59,11 +59,12 @@ def gather_row_kv(k_cache, v_cache, block_table_row, k_len: int):
 
 def paged_attention(q, k_cache, v_cache, block_table, q_starts, q_lens, k_lens, q_pos_offsets,
                     scale: float, is_causal: bool = True, num_kv_heads: int | None = None,
-                    dtype=np.float64, rows=None):
+                    dtype=np.float64, rows=None, heads=None):
     """Reference paged attention. Returns (o [total_q, HQ, D], lse [total_q, HQ]) in `dtype`.
 
     Inputs may be torch tensors or numpy arrays; bf16/fp16 inputs are upcast
-    exactly. Tokens of rows not listed in `rows` (default: all) stay NaN.
+    exactly. Entries of rows not listed in `rows` and of query heads not listed
+    in `heads` (default: all) stay NaN.
     """
     q = _as_np(q, dtype)
     k_cache = _as_np(k_cache, dtype)
@@ -89,7 +90,7 @@ def paged_attention(q, k_cache, v_cache, block_table, q_starts, q_lens, k_lens, 
         allowed = np.ones((nq, n_keys), dtype=bool)
         if is_causal:
             allowed = (qp + np.arange(nq))[:, None] >= np.arange(n_keys)[None, :]
-        for h in range(hq):
+        for h in (range(hq) if heads is None else heads):
             kvh = h // group
             s = (q[qs:qs + nq, h] @ k[:, kvh].T) * dtype(scale)
             s = np.where(allowed, s, -np.inf)

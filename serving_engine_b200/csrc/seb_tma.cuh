@@ -18,6 +18,12 @@ namespace seb {
 int kv_tensor_map(CUtensorMap* out, const void* base, int dtype, int64_t num_blocks, int num_kv_heads,
                   int head_dim);
 
+// General 3-D map of 16-bit elements with 128-byte swizzling: dims (innermost
+// first) in elements, strides of dims 1 and 2 in bytes, box in elements
+// (box[0] * 2 <= 128). Cached like kv_tensor_map.
+int tensor_map_3d(CUtensorMap* out, const void* base, int dtype, const uint64_t dims[3],
+                  const uint64_t strides[2], const uint32_t box[3]);
+
 __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map, int x, int y, int z,
                                             uint32_t bar) {
   asm volatile(

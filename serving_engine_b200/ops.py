@@ -257,3 +257,75 @@ def paged_decode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, 
     LAUNCHES[0] += 2 if ws_bytes > 0 else 1  # split pass (+ combine pass when splits > 1)
     _after(dev)
     return out, lse
+
+
+# -------------------------------------------------------------- paged prefill
+PREFILL_HEAD_DIMS = (64, 128)
+PREFILL_GROUPS = (1, 2, 4, 8, 16)
+
+
+def prefill_supported(q: torch.Tensor, num_q_heads: int, num_kv_heads: int) -> bool:
+    """Whether the tcgen05 chunked-prefill kernel covers this dtype and shape."""
+    if q.dtype not in (torch.bfloat16, torch.float16) or q.dim() != 3:
+        return False
+    if num_kv_heads <= 0 or num_q_heads % num_kv_heads:
+        return False
+    d = q.shape[2]
+    return (d in PREFILL_HEAD_DIMS and num_q_heads // num_kv_heads in PREFILL_GROUPS and q.stride(2) == 1
+            and q.stride(0) % 8 == 0 and q.stride(1) % 8 == 0 and q.data_ptr() % 16 == 0
+            and q.stride(1) >= d and q.stride(0) >= q.stride(1) * num_q_heads)
+
+
+def paged_prefill(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, block_table: torch.Tensor,
+                  q_starts: torch.Tensor, q_lens: torch.Tensor, k_lens: torch.Tensor, q_pos_offsets: torch.Tensor,
+                  num_q_heads: int, num_kv_heads: int, scale: float, is_causal: bool = True, *,
+                  max_q_len: int, rows: torch.Tensor | None = None, num_prefill_rows: int | None = None,
+                  out: torch.Tensor | None = None, lse: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor]:
+    """Chunked-prefill paged attention on tcgen05 tensor cores for the listed rows
+    (default: every row). max_q_len: host-known bound of those rows' q_lens."""
+    dev = _require_cuda("paged_prefill", q, k_cache, v_cache, block_table, q_starts, q_lens, k_lens, q_pos_offsets)
+    if not prefill_supported(q, num_q_heads, num_kv_heads):
+        raise ValueError("paged_prefill: needs bf16/fp16 q [total_query, heads, 64|128] with 16-byte aligned rows "
+                         "and a GQA group of 1, 2, 4, 8 or 16")
+    total_q, hq, d = q.shape
+    if hq != num_q_heads:
+        raise ValueError(f"paged_prefill: q has {hq} heads, num_q_heads={num_q_heads}")
+    if k_cache.dim() != 4 or k_cache.shape[1] != BLOCK_SIZE or tuple(k_cache.shape[2:]) != (num_kv_heads, d):
+        raise ValueError(f"paged_prefill: k_cache must be [num_blocks, {BLOCK_SIZE}, {num_kv_heads}, {d}]")
+    if v_cache.shape != k_cache.shape or not (k_cache.is_contiguous() and v_cache.is_contiguous()):
+        raise ValueError("paged_prefill: k_cache and v_cache must be contiguous and of equal shape")
+    if not (q.dtype == k_cache.dtype == v_cache.dtype):
+        raise ValueError("paged_prefill: dtype mismatch")
+    for name, t in (("block_table", block_table), ("q_starts", q_starts), ("q_lens", q_lens), ("k_lens", k_lens),
+                    ("q_pos_offsets", q_pos_offsets)):
+        if t.dtype != torch.int32:
+            raise ValueError(f"paged_prefill: {name} must be int32")
+    n_rows = q_starts.numel()
+    if block_table.dim() != 2 or block_table.shape[0] != n_rows or block_table.stride(1) != 1:
+        raise ValueError("paged_prefill: block_table must be [rows, max_blocks] with unit column stride")
+    if rows is not None:
+        rows = rows.to(torch.int32).contiguous()
+        num_prefill_rows = rows.numel() if num_prefill_rows is None else num_prefill_rows
+    elif num_prefill_rows is None:
+        num_prefill_rows = n_rows
+    if out is None:
+        out = torch.empty_like(q)
+    if lse is None:
+        lse = torch.empty((total_q, num_q_heads), dtype=torch.float32, device=dev)
+    if out.stride(2) != 1 or out.stride(0) % 8 or out.stride(1) % 8 or out.data_ptr() % 16:
+        raise ValueError("paged_prefill: out rows must be 16-byte aligned")
+    if num_prefill_rows == 0 or max_q_len == 0 or block_table.shape[1] == 0:
+        return out, lse
+    q_starts, q_lens, k_lens, q_pos_offsets = (t.contiguous() for t in (q_starts, q_lens, k_lens, q_pos_offsets))
+    st = lib().seb_paged_prefill(
+        q.data_ptr(), q.stride(0), q.stride(1), k_cache.data_ptr(), v_cache.data_ptr(), k_cache.shape[0],
+        block_table.data_ptr(), block_table.stride(0), block_table.shape[1],
+        q_starts.data_ptr(), q_lens.data_ptr(), k_lens.data_ptr(), q_pos_offsets.data_ptr(), n_rows, total_q,
+        rows.data_ptr() if rows is not None else None, int(num_prefill_rows), int(max_q_len),
+        num_q_heads, num_kv_heads, d, dtype_code(q), float(scale), 1 if is_causal else 0,
+        out.data_ptr(), out.stride(0), out.stride(1), lse.data_ptr(), lse.stride(0),
+        err_word(dev).data_ptr(), _stream(dev))
+    check("seb_paged_prefill", st)
+    LAUNCHES[0] += 1
+    _after(dev)
+    return out, lse

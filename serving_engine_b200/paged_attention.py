@@ -69,7 +69,9 @@ class PackedMetadata:
     """Host side of one step's metadata: every int32 array in one buffer.
 
     Layout: q_lens[R] | k_lens[R] | q_starts[R] | q_pos_offsets[R] |
-    block_table[R, W] | item_row[total_query]. ``upload`` issues ONE
+    block_table[R, W] | item_row[total_query] | decode tokens[Nd] |
+    decode rows[Nd] | prefill rows[Np], where decode rows are those with
+    q_len == 1 and prefill rows those with q_len > 1. ``upload`` issues ONE
     host-to-device copy (pinned) and returns the metadata dict.
     """
 
@@ -81,7 +83,9 @@ class PackedMetadata:
         total_query = int(q_lens_np.sum())
         o_bt = 4 * rows
         o_items = o_bt + rows * width
-        packed = torch.zeros(o_items + total_query, dtype=torch.int32)
+        n_dec = int((q_lens_np == 1).sum())
+        n_pre = int((q_lens_np > 1).sum())
+        packed = torch.zeros(o_items + total_query + 2 * n_dec + n_pre, dtype=torch.int32)
         a = packed.numpy()
         a[0:rows] = q_lens_np
         a[rows:2 * rows] = k_lens
@@ -97,7 +101,18 @@ class PackedMetadata:
             self.max_block_id = int(flat.max())
         else:
             self.max_block_id = -1
-        a[o_items:] = np.repeat(np.arange(rows, dtype=np.int32), q_lens_np)
+        a[o_items:o_items + total_query] = np.repeat(np.arange(rows, dtype=np.int32), q_lens_np)
+        # decode items (rows with q_len == 1: token, row) and prefill rows (q_len > 1)
+        dec_rows = np.nonzero(q_lens_np == 1)[0].astype(np.int32)
+        pre_rows = np.nonzero(q_lens_np > 1)[0].astype(np.int32)
+        starts_np = a[2 * rows:3 * rows]
+        o_dec = o_items + total_query
+        a[o_dec:o_dec + len(dec_rows)] = starts_np[dec_rows]
+        a[o_dec + len(dec_rows):o_dec + 2 * len(dec_rows)] = dec_rows
+        a[o_dec + 2 * len(dec_rows):] = pre_rows
+        self.num_decode = len(dec_rows)
+        self.num_prefill = len(pre_rows)
+        self.max_prefill_q_len = int(q_lens_np[pre_rows].max()) if len(pre_rows) else 0
         self.host = packed
         self.rows, self.width, self.total_query = rows, width, total_query
         self.max_q_len = int(q_lens_np.max()) if rows else 0
@@ -120,6 +135,8 @@ class PackedMetadata:
             buf = self.host.clone()
         rows, width = self.rows, self.width
         o = 4 * rows
+        o_dec = o + rows * width + self.total_query
+        nd = self.num_decode
         return {
             "q_lens": buf[0:rows],
             "k_lens": buf[rows:2 * rows],
@@ -130,9 +147,13 @@ class PackedMetadata:
             "total_query": self.total_query,
             # host-known extras (not in the reference's dict)
             "max_q_len": self.max_q_len,
-            "item_row": buf[o + rows * width:],
+            "item_row": buf[o + rows * width:o + rows * width + self.total_query],
             "max_block_id": self.max_block_id,
             "max_k_len": self.max_k_len,
+            "decode_tokens": buf[o_dec:o_dec + nd],
+            "decode_rows": buf[o_dec + nd:o_dec + 2 * nd],
+            "prefill_rows": buf[o_dec + 2 * nd:o_dec + 2 * nd + self.num_prefill],
+            "max_prefill_q_len": self.max_prefill_q_len,
         }
 
 
@@ -148,6 +169,11 @@ def paged_flash_attention(q, k_cache, v_cache, metadata, num_q_heads, num_kv_hea
     block_size, num_kv_heads, head_dim] (not pre-gathered); metadata as built by
     build_paged_batch_metadata. Returns (o like q, l fp32 [total_query,
     num_q_heads]) where l is the log-sum-exp of the scaled scores (natural log).
+
+    Rows with q_len == 1 go to the split-K decode kernel, rows with q_len > 1 to
+    the tcgen05 chunked-prefill kernel (bf16/fp16, head_dim 64/128). Other dtypes
+    and shapes, and metadata dicts without the host-side row split, run every
+    token through the decode kernel, which computes any row exactly.
     """
     rows = metadata["q_lens"].shape[0]
     width = int(metadata["block_table_row_stride"])
@@ -161,6 +187,21 @@ def paged_flash_attention(q, k_cache, v_cache, metadata, num_q_heads, num_kv_hea
     lse = torch.empty((q.shape[0], num_q_heads), dtype=torch.float32, device=q.device)
     if rows == 0 or q.shape[0] == 0:
         return o, lse
-    return ops.paged_decode(q, k_cache, v_cache, metadata["block_table"], metadata["q_starts"], metadata["k_lens"],
-                            metadata["q_pos_offsets"], num_q_heads, num_kv_heads, scale, is_causal,
-                            item_row=metadata.get("item_row"), out=o, lse=lse)
+    common = (metadata["block_table"],)
+    split = "prefill_rows" in metadata and ops.prefill_supported(q, num_q_heads, num_kv_heads) and (
+        o.stride(0) % 8 == 0 and o.stride(1) % 8 == 0 and o.data_ptr() % 16 == 0)
+    if not split:
+        return ops.paged_decode(q, k_cache, v_cache, *common, metadata["q_starts"], metadata["k_lens"],
+                                metadata["q_pos_offsets"], num_q_heads, num_kv_heads, scale, is_causal,
+                                item_row=metadata.get("item_row"), out=o, lse=lse)
+    n_dec = metadata["decode_tokens"].numel()
+    n_pre = metadata["prefill_rows"].numel()
+    if n_dec:
+        ops.paged_decode(q, k_cache, v_cache, *common, metadata["q_starts"], metadata["k_lens"],
+                         metadata["q_pos_offsets"], num_q_heads, num_kv_heads, scale, is_causal,
+                         item_query=metadata["decode_tokens"], item_row=metadata["decode_rows"], out=o, lse=lse)
+    if n_pre:
+        ops.paged_prefill(q, k_cache, v_cache, *common, metadata["q_starts"], metadata["q_lens"], metadata["k_lens"],
+                          metadata["q_pos_offsets"], num_q_heads, num_kv_heads, scale, is_causal,
+                          max_q_len=metadata["max_prefill_q_len"], rows=metadata["prefill_rows"], out=o, lse=lse)
+    return o, lse

@@ -1,0 +1,139 @@
+"""Chunked-prefill paged attention on tcgen05 tensor cores (through the C ABI)
+against the CPU oracle, and the q_len-based dispatch of paged_flash_attention.
+
+Tolerance: bf16/fp16 O within 2e-3 of the fp64 oracle on the same 16-bit
+values plus half an ulp of the stored output; LSE within 1e-3.
+"""
+import math
+
+import numpy as np
+import pytest
+import torch
+
+from oracle.paged_attention import paged_attention
+from serving_engine_b200 import check_device_errors, ops, paged_flash_attention, workloads
+from serving_engine_b200.paged_attention import metadata_from_lists
+from tests.test_paged_decode_gpu import assert_close, assert_out_close
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+def make_batch(rows, hq, hkv, d, dtype, seed, shared_prefix_blocks=0, nan_tail=False):
+    """rows: list of (q_len, q_pos_offset); k_len = q_pos_offset + q_len."""
+    gen = torch.Generator().manual_seed(seed)
+    need = [math.ceil((ql + qp) / 16) for ql, qp in rows]
+    nb = sum(need) + 8
+    perm = torch.randperm(nb, generator=gen).tolist()
+    tables, p = [], 0
+    for n in need:
+        tables.append(perm[p:p + n])
+        p += n
+    if shared_prefix_blocks:
+        for t in tables[1:]:
+            k = min(shared_prefix_blocks, len(t) - 1, len(tables[0]) - 1)
+            t[:k] = tables[0][:k]
+    tq = sum(r[0] for r in rows)
+    b = workloads.PagedBatch(q=torch.randn(tq, hq, d, generator=gen).to(dtype),
+                             k_cache=torch.randn(nb, 16, hkv, d, generator=gen).to(dtype),
+                             v_cache=torch.randn(nb, 16, hkv, d, generator=gen).to(dtype), block_tables=tables,
+                             q_lens=[r[0] for r in rows], k_lens=[sum(r) for r in rows],
+                             q_pos_offsets=[r[1] for r in rows], num_q_heads=hq, num_kv_heads=hkv,
+                             scale=1 / math.sqrt(d))
+    if nan_tail:
+        for r, t in enumerate(tables):
+            k = b.k_lens[r]
+            if k % 16:
+                b.k_cache[t[(k - 1) // 16], k % 16:] = float("nan")
+                b.v_cache[t[(k - 1) // 16], k % 16:] = float("nan")
+    return b
+
+
+def run_prefill(b, is_causal=True):
+    md = metadata_from_lists(b.q_lens, b.k_lens, b.q_starts, b.q_pos_offsets, b.block_tables, DEV)
+    o, lse = ops.paged_prefill(b.q.to(DEV), b.k_cache.to(DEV), b.v_cache.to(DEV), md["block_table"], md["q_starts"],
+                               md["q_lens"], md["k_lens"], md["q_pos_offsets"], b.num_q_heads, b.num_kv_heads, b.scale,
+                               is_causal, max_q_len=max(b.q_lens))
+    torch.cuda.synchronize()
+    check_device_errors()
+    return o.float().cpu().numpy(), lse.cpu().numpy()
+
+
+def oracle(b, is_causal=True, **kw):
+    md = b.metadata("cpu")
+    return paged_attention(b.q, b.k_cache, b.v_cache, md["block_table"], md["q_starts"], md["q_lens"], md["k_lens"],
+                           md["q_pos_offsets"], b.scale, is_causal, **kw)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("hq,hkv", [(32, 8), (8, 8), (16, 8), (32, 4), (16, 1)])
+@pytest.mark.parametrize("d", [64, 128])
+def test_prefill_shapes_vs_oracle(dtype, hq, hkv, d):
+    rows = [(70, 0), (33, 100), (128, 37), (5, 300)]
+    b = make_batch(rows, hq, hkv, d, dtype, seed=hq + hkv * 3 + d)
+    o, lse = run_prefill(b)
+    o_ref, lse_ref = oracle(b)
+    assert_close(o, lse, o_ref, lse_ref, dtype)
+
+
+def test_prefill_long_chunk_shared_prefix():
+    """Config-3 pattern at reduced size: rows share prefix blocks, then prefill a chunk."""
+    rows = [(200, 512)] * 4
+    b = make_batch(rows, 32, 8, 128, torch.bfloat16, seed=5, shared_prefix_blocks=32)
+    o, lse = run_prefill(b)
+    o_ref, lse_ref = oracle(b)
+    assert_close(o, lse, o_ref, lse_ref, torch.bfloat16)
+
+
+def test_prefill_noncausal_and_partial_blocks():
+    rows = [(40, 0), (17, 9), (64, 63)]
+    b = make_batch(rows, 16, 4, 128, torch.bfloat16, seed=7)
+    o, lse = run_prefill(b, is_causal=False)
+    o_ref, lse_ref = oracle(b, is_causal=False)
+    assert_close(o, lse, o_ref, lse_ref, torch.bfloat16)
+
+
+def test_prefill_nan_pool_tail_does_not_leak():
+    rows = [(45, 3), (30, 50)]
+    b = make_batch(rows, 32, 8, 128, torch.bfloat16, seed=9, nan_tail=True)
+    o, lse = run_prefill(b)
+    assert np.isfinite(o).all()
+    clean = make_batch(rows, 32, 8, 128, torch.bfloat16, seed=9)
+    o_ref, lse_ref = oracle(clean)
+    assert_close(o, lse, o_ref, lse_ref, torch.bfloat16)
+
+
+def test_config3_full_size_sampled():
+    """Full config 3: 16 rows x 512-token chunks after a shared 2048-token prefix,
+    32/8 heads, D=128; two rows x one GQA group checked against the oracle, all
+    outputs finite."""
+    b = workloads.config3(seed=1)
+    md = metadata_from_lists(b.q_lens, b.k_lens, b.q_starts, b.q_pos_offsets, b.block_tables, DEV)
+    o, lse = ops.paged_prefill(b.q.to(DEV), b.k_cache.to(DEV), b.v_cache.to(DEV), md["block_table"], md["q_starts"],
+                               md["q_lens"], md["k_lens"], md["q_pos_offsets"], 32, 8, b.scale, True,
+                               max_q_len=512)
+    torch.cuda.synchronize()
+    check_device_errors()
+    assert torch.isfinite(o.float()).all() and torch.isfinite(lse).all()
+    heads = [4, 5, 6, 7]
+    o_ref, lse_ref = oracle(b, rows=[0, 11], heads=heads)
+    for r in (0, 11):
+        sl = slice(r * 512, (r + 1) * 512)
+        assert_out_close(o[sl][:, heads].float().cpu().numpy(), o_ref[sl][:, heads], torch.bfloat16)
+        np.testing.assert_allclose(lse[sl][:, heads].cpu().numpy(), lse_ref[sl][:, heads], atol=1e-3, rtol=0)
+
+
+def test_dispatch_mixed_decode_and_prefill_rows():
+    """paged_flash_attention sends q_len == 1 rows to the decode kernel and
+    q_len > 1 rows to the tcgen05 prefill kernel; together they match the oracle."""
+    rows = [(1, 300), (77, 0), (1, 15), (130, 900), (1, 0), (16, 16)]
+    b = make_batch(rows, 32, 8, 128, torch.bfloat16, seed=13)
+    md = metadata_from_lists(b.q_lens, b.k_lens, b.q_starts, b.q_pos_offsets, b.block_tables, DEV)
+    assert md["decode_tokens"].numel() == 3 and md["prefill_rows"].numel() == 3
+    launches = ops.LAUNCHES[0]
+    o, lse = paged_flash_attention(b.q.to(DEV), b.k_cache.to(DEV), b.v_cache.to(DEV), md, 32, 8, b.scale)
+    torch.cuda.synchronize()
+    check_device_errors()
+    assert ops.LAUNCHES[0] - launches >= 2
+    o_ref, lse_ref = oracle(b)
+    assert_close(o.float().cpu().numpy(), lse.cpu().numpy(), o_ref, lse_ref, torch.bfloat16)
