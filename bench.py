@@ -52,6 +52,8 @@ def parse_args():
     ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--workload", default="decode", choices=["decode", "prefill"],
+                    help="decode: config 2 (the headline line); prefill: config 3")
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--batch", type=int, default=64)
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -347,6 +349,74 @@ def run_reference(args, device):
     }
 
 
+# ------------------------------------------------------------ config 3 prefill
+def prefill_flops(b) -> float:
+    """Causal, unmasked (query, key) pairs only: 4 * D per pair per q head."""
+    total = 0
+    for ql, qp, kl in zip(b.q_lens, b.q_pos_offsets, b.k_lens):
+        total += sum(min(kl, qp + i + 1) for i in range(ql))
+    return 4.0 * b.head_dim * b.num_q_heads * total
+
+
+def run_prefill_workload(args, device):
+    """Config 3: 16 rows share a 2040-token prefix (127 full blocks + one 8-token
+    partial block); per step each row copies the partial block into a fresh
+    block (CoW), appends its 512-token chunk's K/V and runs chunked-prefill
+    attention (tcgen05)."""
+    from serving_engine_b200 import ops, paged_flash_attention, workloads
+    from serving_engine_b200.paged_attention import metadata_from_lists
+
+    b = workloads.config3(seed=args.seed, prefix_len=2040, fill=str(device))
+    md = metadata_from_lists(b.q_lens, b.k_lens, b.q_starts, b.q_pos_offsets, b.block_tables, device)
+    q = b.q.to(device)
+    nk, nv = b.extra["new_k"].to(device), b.extra["new_v"].to(device)
+    slots = b.extra["slot_mapping"].to(device)
+    pool = torch.stack([b.k_cache, b.v_cache]).unsqueeze(0)  # one layer [1, 2, NB, 16, H, D]
+    kc, vc = pool[0, 0], pool[0, 1]
+    src = torch.tensor(b.extra["cow_src"], dtype=torch.int64, device=device)
+    dst = torch.tensor(b.extra["cow_dst"], dtype=torch.int64, device=device)
+    flops = prefill_flops(b)
+    stream = torch.cuda.current_stream(device)
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+    t_cow = t_app = t_att = 0.0
+    for it in range(max(args.warmup, 3) + args.steps):
+        timed = it >= max(args.warmup, 3)
+        ev[0].record(stream)
+        ops.copy_blocks(pool, src, dst)
+        ev[1].record(stream)
+        ops.kv_append(nk, nv, kc, vc, slots)
+        ev[2].record(stream)
+        paged_flash_attention(q, kc, vc, md, 32, 8, b.scale)
+        ev[3].record(stream)
+        if timed:
+            torch.cuda.synchronize(device)
+            t_cow += ev[0].elapsed_time(ev[1])
+            t_app += ev[1].elapsed_time(ev[2])
+            t_att += ev[2].elapsed_time(ev[3])
+    ops.check_device_errors(device)
+    n = args.steps
+    att_ms, cow_ms, app_ms = t_att / n, t_cow / n, t_app / n
+    tflops = flops / (att_ms * 1e-3) / 1e12
+    peaks_path = REPO / "MEASURED_PEAKS.json"
+    pk = json.loads(peaks_path.read_text()) if peaks_path.exists() else {"bf16_tflops": 1590.0}
+    app_bytes = 2 * 2 * nk.numel() * nk.element_size()
+    cow_bytes = 2 * 2 * len(b.extra["cow_dst"]) * 16 * 8 * 128 * 2
+    return {
+        "metric": "chunked-prefill attention TFLOP/s (config 3)", "value": round(tflops, 1), "unit": "TFLOP/s",
+        "n_gpus": 1, "steps": n, "warmup": args.warmup, "ms_per_step": round(att_ms + cow_ms + app_ms, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": "config 3: 16 rows, shared 2040-token prefix, 512-token causal chunks, 32q/8kv, D=128",
+                   "attention_gflop": round(flops / 1e9, 1)},
+        "breakdown_ms": {"cow_copy_blocks": round(cow_ms, 4), "kv_append": round(app_ms, 4),
+                         "prefill_attention": round(att_ms, 4)},
+        "bandwidth_gbs": {"kv_append": round(app_bytes / (app_ms * 1e-3) / 1e9, 1),
+                          "cow_copy_blocks": round(cow_bytes / (cow_ms * 1e-3) / 1e9, 1)},
+        "roofline": {"bound": "tensor", "achieved": round(tflops, 1), "peak": pk.get("bf16_tflops"),
+                     "unit": "TFLOP/s", "frac": round(tflops / pk.get("bf16_tflops", 1590.0), 4),
+                     "peak_source": "measured burst (MEASURED_PEAKS.json bf16_tflops)", "traffic": None},
+    }
+
+
 def main():
     args = parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -363,6 +433,10 @@ def main():
 
     device = torch.device("cuda", local_rank)
     torch.cuda.set_device(device)
+    if args.workload == "prefill":
+        if rank == 0:
+            print(json.dumps(run_prefill_workload(args, device)), flush=True)
+        return
     dist = None
     if world > 1:
         import datetime
