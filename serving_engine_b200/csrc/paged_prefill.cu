@@ -15,11 +15,13 @@
 //   warp 1     owns TMEM (512 columns: S double buffer at 0 and 128, O at 256)
 //              and issues the MMAs from one thread: S = Q K^T (M=128, N=128,
 //              K=head_dim) and O += P V (M=128, N=head_dim, K=128 keys);
-//   warps 2-5  one TMEM lane (= tile row) per thread: read S, mask, online
-//              softmax with a lazily rescaled reference max (O and l are only
-//              rescaled when a block max exceeds it by 2^8), write P as bf16 to
-//              a swizzled shared-memory tile, and finally normalise O, store it
-//              and the LSE.
+//   warps 2-9  two softmax warpgroups; a thread owns half of one tile row
+//              (TMEM lane): read its 64 scores, mask boundary tiles, agree on
+//              the row max with its partner thread through shared memory,
+//              online softmax with a lazily rescaled reference max (O and l are
+//              only rescaled when a block max exceeds it by 2^8), write P as
+//              bf16 to a swizzled shared-memory tile, and finally normalise its
+//              half of O, store it and the LSE.
 // P V is split into a 16-bit high part and its 16-bit remainder for tiles
 // whose rows see fewer than kSplitBelow keys (early positions of a prompt),
 // where one rounding of P would cost more than the output tolerance.
@@ -40,7 +42,7 @@ constexpr float kLog2ep = 1.44269504088896340736f;
 constexpr unsigned kFullMask = 0xffffffffu;
 constexpr int kBM = 128;        // MMA rows per CTA
 constexpr int kBN = 128;        // keys per KV tile
-constexpr int kThreads = 192;   // producer, MMA, 4 softmax warps
+constexpr int kThreads = 320;   // producer, MMA, 8 softmax warps (2 warpgroups)
 constexpr int kRing = 2;        // K/V ring depth
 constexpr int kTmemCols = 512;
 constexpr int kColS = 0;        // S buffers at columns 0 and 128
@@ -82,9 +84,13 @@ struct PrefillLayout {
   static constexpr int oK = oQ + kTileQ;
   static constexpr int oV = oK + kRing * kTileKV;
   static constexpr int oP = oV + kRing * kTileKV;
-  static constexpr int oPlo = oP + kTileP;  // P's 16-bit remainder (split tiles)
-  static constexpr int oBar = oPlo + kTileP;
-  static constexpr int kBytes = oBar + 256;
+  // P's 16-bit remainder (split tiles): in the K stage of the same tile when a
+  // K tile can hold it (S of that tile has consumed K by then), else its own.
+  static constexpr bool kPloInK = kTileKV >= kTileP;
+  static constexpr int oPloSep = oP + kTileP;
+  static constexpr int oBar = oPloSep + (kPloInK ? 0 : kTileP);
+  static constexpr int oX = oBar + 256;  // row max / sum exchange between the two softmax warpgroups
+  static constexpr int kBytes = oX + 3 * 128 * 4 * 2;
 };
 
 // mbarrier slots
@@ -100,6 +106,17 @@ enum {
   kBarDone = 13,
   kNumBars = 14
 };
+
+// 2^x by the MUFU instruction (ex2.approx.ftz: 2^-22 relative error, -inf -> +0).
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+__device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
 
 __device__ __forceinline__ bool wait_or_flag(uint32_t bar, uint32_t parity, bool& failed) {
   if (failed) return false;
@@ -165,7 +182,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (ntiles == 0) {
     // No visible keys: the reference's loop never runs, O = 0/0, LSE = -inf.
-    if (row_valid) {
+    if (row_valid && warp < 6) {
       T* op = reinterpret_cast<T*>(p.out) + (int64_t)(q_start + qi) * p.o_st + (int64_t)(kvh * G + gh) * p.o_sh;
       for (int d = 0; d < D; ++d) op[d] = Elem<T>::from_float(__int_as_float(0x7fc00000));
       p.lse[(int64_t)(q_start + qi) * p.lse_st + kvh * G + gh] = -INFINITY;
@@ -184,9 +201,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(bar + 8 * (kBarSFull + b), 1);
-      mbar_init(bar + 8 * (kBarSFree + b), 4);
+      mbar_init(bar + 8 * (kBarSFree + b), 8);
     }
-    mbar_init(bar + 8 * kBarPFull, 4);
+    mbar_init(bar + 8 * kBarPFull, 8);
     mbar_init(bar + 8 * kBarOFull, 1);
     mbar_init(bar + 8 * kBarDone, 1);
     fence_mbar_init();
@@ -302,9 +319,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           tc::mma_ss(tmem + kColO, a, b, idesc_pv, j > 0 || kk > 0);
         }
         if (split) {
+          const uint32_t plo = base + (L::kPloInK ? L::oK + s * L::kTileKV : L::oPloSep);
 #pragma unroll
           for (int kk = 0; kk < kBN / 16; ++kk) {
-            const uint64_t a = tc::smem_desc_sw128(base + L::oPlo + (kk >> 2) * L::kPanel + (kk & 3) * 32, 16, 1024);
+            const uint64_t a = tc::smem_desc_sw128(plo + (kk >> 2) * L::kPanel + (kk & 3) * 32, 16, 1024);
             const uint64_t b = tc::smem_desc_sw128(base + L::oV + s * L::kTileKV + kk * 2048, L::kPanel, 1024);
             tc::mma_ss(tmem + kColO, a, b, idesc_pv, true);
           }
@@ -320,73 +338,98 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_wait_bounded(bar + 8 * kBarDone, 0, 1u << 20);
   } else {
     // ------------------------------------------------------------ softmax
+    // Two warpgroups share each tile row: `half` 0 owns keys / O columns 0-63,
+    // half 1 owns 64-127. Warps w and w+4 see the same TMEM lanes (w % 4).
+    const int half = (warp - 2) >> 2;
     const uint32_t taddr = tmem + ((uint32_t)(q4 * 32) << 16);
     const int pos = qpos0 + qi;
     const int vis = row_valid ? (p.causal ? min(ceil16, pos + 1) : ceil16) : 0;
+    const float c = p.scale_log2;
+    float* xchg = reinterpret_cast<float*>(sbase + L::oX);  // [parity][half][128] maxima, then [half][128] sums
     float m_ref = -INFINITY;
     float l = 0.f;
-    const uint32_t prow_addr = L::oP + m * 128;
+    char* ph = sbase + L::oP + half * L::kPanel + m * 128;
+    // After a failed (timed-out) wait the loop keeps its shape with the waits
+    // skipped, so both warpgroups still meet at every named barrier.
     for (int j = 0; j < ntiles; ++j) {
       const int b = j & 1;
-      if (!wait_or_flag(bar + 8 * (kBarSFull + b), (j >> 1) & 1, failed)) break;
+      wait_or_flag(bar + 8 * (kBarSFull + b), (j >> 1) & 1, failed);
       tc::fence_after_sync();
-      float x[kBN];
-#pragma unroll
-      for (int c = 0; c < kBN / 32; ++c) {
+      float x[64];
+      {
         float v[32];
-        tc::tmem_ld32(taddr + kColS + b * kBN + 32 * c, v);
+        tc::tmem_ld32(taddr + kColS + b * kBN + half * 64, v);
 #pragma unroll
-        for (int i = 0; i < 32; ++i) x[32 * c + i] = v[i];
+        for (int i = 0; i < 32; ++i) x[i] = v[i];
+        tc::tmem_ld32(taddr + kColS + b * kBN + half * 64 + 32, v);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) x[32 + i] = v[i];
       }
       tc::tmem_wait_ld();
       tc::fence_before_sync();
       __syncwarp();
       if (lane == 0) mbar_arrive(bar + 8 * (kBarSFree + b));
 
-      const int kbase = j * kBN;
-      float mb = -INFINITY;
+      // Tiles every valid row sees in full need no mask: scores stay raw and
+      // the scale folds into the exponent's FMA. Boundary tiles are masked and
+      // scaled here (keys past the row's visible range: -inf; zero-padded keys
+      // of the last block: 0).
+      const bool full = (j + 1) * kBN <= min_vis && (j + 1) * kBN <= k_len;
+      float mloc = -INFINITY, cm = c;
+      if (full) {
 #pragma unroll
-      for (int c = 0; c < kBN; ++c) {
-        const int key = kbase + c;
-        float v = x[c] * p.scale_log2;
-        if (key >= vis) v = -INFINITY;
-        else if (key >= k_len) v = 0.f;  // zero-padded key of the last block
-        x[c] = v;
-        mb = fmaxf(mb, v);
+        for (int i = 0; i < 64; ++i) mloc = fmaxf(mloc, x[i]);
+        mloc *= c;
+      } else {
+        const int kbase = j * kBN + half * 64;
+#pragma unroll
+        for (int i = 0; i < 64; ++i) {
+          const int key = kbase + i;
+          float v = x[i] * c;
+          if (key >= vis) v = -INFINITY;
+          else if (key >= k_len) v = 0.f;
+          x[i] = v;
+          mloc = fmaxf(mloc, v);
+        }
+        cm = 1.f;
       }
+      // Row max over both halves.
+      xchg[(j & 1) * 256 + half * 128 + m] = mloc;
+      named_bar_sync(1 + q4, 64);
+      const float mb = fmaxf(mloc, xchg[(j & 1) * 256 + (1 - half) * 128 + m]);
       const bool need = mb > m_ref + kLazyThreshold;
       // PV(j-1) must be complete: it reads the P buffers and accumulates O.
-      if (j > 0 && !wait_or_flag(bar + 8 * kBarOFull, (j - 1) & 1, failed)) break;
+      if (j > 0) wait_or_flag(bar + 8 * kBarOFull, (j - 1) & 1, failed);
       tc::fence_after_sync();
       float factor = 1.f;
       if (need) {
-        factor = exp2f(m_ref - mb);  // 0 while m_ref is -inf
+        factor = fast_exp2(m_ref - mb);  // 0 while m_ref is -inf
         l *= factor;
         m_ref = mb;
       }
       if (j > 0 && __any_sync(kFullMask, need)) {
         // warp-collective: rows that keep their reference max scale by 1
 #pragma unroll
-        for (int c = 0; c < D / 32; ++c) {
+        for (int cc = 0; cc < D / 64; ++cc) {
           float o[32];
-          tc::tmem_ld32(taddr + kColO + 32 * c, o);
+          const uint32_t a = taddr + kColO + half * (D / 2) + 32 * cc;
+          tc::tmem_ld32(a, o);
           tc::tmem_wait_ld();
 #pragma unroll
           for (int i = 0; i < 32; ++i) o[i] *= factor;
-          tc::tmem_st32(taddr + kColO + 32 * c, o);
+          tc::tmem_st32(a, o);
         }
         tc::tmem_wait_st();
       }
-      const float m_use = m_ref == -INFINITY ? 0.f : m_ref;
-      char* ph = sbase + prow_addr;
-      char* pl = sbase + L::oPlo + m * 128;
+      const float neg_m = m_ref == -INFINITY ? 0.f : -m_ref;
+      char* pl = sbase + (L::kPloInK ? L::oK + (j & 1) * L::kTileKV : L::oPloSep) + half * L::kPanel + m * 128;
 #pragma unroll
-      for (int ch = 0; ch < kBN / 8; ++ch) {
+      for (int ch = 0; ch < 8; ++ch) {
         uint32_t hi[4], lo[4];
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-          const float a0 = exp2f(x[8 * ch + 2 * e] - m_use);
-          const float a1 = exp2f(x[8 * ch + 2 * e + 1] - m_use);
+          const float a0 = fast_exp2(fmaf(x[8 * ch + 2 * e], cm, neg_m));
+          const float a1 = fast_exp2(fmaf(x[8 * ch + 2 * e + 1], cm, neg_m));
           l += a0 + a1;
           hi[e] = Mma<T>::pack(a0, a1);
           if (split) {
@@ -394,8 +437,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             lo[e] = Mma<T>::pack(a0 - f.x, a1 - f.y);
           }
         }
-        const int panel = ch >> 3;
-        const int off = panel * L::kPanel + ((((ch & 7) ^ (m & 7))) << 4);
+        const int off = ((ch ^ (m & 7))) << 4;
         *reinterpret_cast<uint4*>(ph + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
         if (split) *reinterpret_cast<uint4*>(pl + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
       }
@@ -405,26 +447,32 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (lane == 0) mbar_arrive(bar + 8 * kBarPFull);
     }
     // ------------------------------------------------------------ epilogue
-    if (!failed && wait_or_flag(bar + 8 * kBarOFull, (ntiles - 1) & 1, failed)) {
-      tc::fence_after_sync();
-      T* op = reinterpret_cast<T*>(p.out) + (int64_t)(q_start + qi) * p.o_st + (int64_t)(kvh * G + gh) * p.o_sh;
+    wait_or_flag(bar + 8 * kBarOFull, (ntiles - 1) & 1, failed);
+    tc::fence_after_sync();
+    xchg[512 + half * 128 + m] = l;
+    named_bar_sync(1 + q4, 64);
+    if (!__any_sync(kFullMask, failed)) {  // warp-uniform: tcgen05.ld is warp-collective
+      const float l_tot = l + xchg[512 + (1 - half) * 128 + m];
+      const float inv = 1.f / l_tot;
+      T* op = reinterpret_cast<T*>(p.out) + (int64_t)(q_start + qi) * p.o_st + (int64_t)(kvh * G + gh) * p.o_sh +
+              half * (D / 2);
 #pragma unroll
-      for (int c = 0; c < D / 32; ++c) {
+      for (int cc = 0; cc < D / 64; ++cc) {
         float o[32];
-        tc::tmem_ld32(taddr + kColO + 32 * c, o);
+        tc::tmem_ld32(taddr + kColO + half * (D / 2) + 32 * cc, o);
         tc::tmem_wait_ld();
         if (row_valid) {
 #pragma unroll
           for (int v8 = 0; v8 < 4; ++v8) {
             uint32_t w[4];
 #pragma unroll
-            for (int e = 0; e < 4; ++e)
-              w[e] = Mma<T>::pack(o[8 * v8 + 2 * e] / l, o[8 * v8 + 2 * e + 1] / l);
-            *reinterpret_cast<uint4*>(op + 32 * c + 8 * v8) = make_uint4(w[0], w[1], w[2], w[3]);
+            for (int e = 0; e < 4; ++e) w[e] = Mma<T>::pack(o[8 * v8 + 2 * e] * inv, o[8 * v8 + 2 * e + 1] * inv);
+            *reinterpret_cast<uint4*>(op + 32 * cc + 8 * v8) = make_uint4(w[0], w[1], w[2], w[3]);
           }
         }
       }
-      if (row_valid) p.lse[(int64_t)(q_start + qi) * p.lse_st + kvh * G + gh] = m_ref * kLn2p + logf(l);
+      if (row_valid && half == 0)
+        p.lse[(int64_t)(q_start + qi) * p.lse_st + kvh * G + gh] = m_ref * kLn2p + logf(l_tot);
     }
   }
 
