@@ -83,28 +83,30 @@ struct PrefillLayout {
   static constexpr int oQ = 0;
   static constexpr int oK = oQ + kTileQ;
   static constexpr int oV = oK + kRing * kTileKV;
-  static constexpr int oP = oV + kRing * kTileKV;
+  static constexpr int oP = oV + kRing * kTileKV;  // two P buffers (tiles j even / odd)
   // P's 16-bit remainder (split tiles): in the K stage of the same tile when a
-  // K tile can hold it (S of that tile has consumed K by then), else its own.
+  // K tile can hold it (S of that tile has consumed K by then), else its own
+  // pair of buffers.
   static constexpr bool kPloInK = kTileKV >= kTileP;
-  static constexpr int oPloSep = oP + kTileP;
-  static constexpr int oBar = oPloSep + (kPloInK ? 0 : kTileP);
+  static constexpr int oPloSep = oP + 2 * kTileP;
+  static constexpr int oBar = oPloSep + (kPloInK ? 0 : 2 * kTileP);
   static constexpr int oX = oBar + 256;  // row max / sum exchange between the two softmax warpgroups
-  static constexpr int kBytes = oX + 3 * 128 * 4 * 2;
+  static constexpr int kBytes = oX + 2 * 128 * 4;
 };
 
 // mbarrier slots
 enum {
   kBarQ = 0,
-  kBarKFull = 1,   // +stage
-  kBarVFull = 3,   // +stage
-  kBarKVEmpty = 5, // +stage
-  kBarSFull = 7,   // +buffer
-  kBarSFree = 9,   // +buffer
-  kBarPFull = 11,
-  kBarOFull = 12,
-  kBarDone = 13,
-  kNumBars = 14
+  kBarKFull = 1,    // +stage
+  kBarVFull = 3,    // +stage
+  kBarKVEmpty = 5,  // +stage
+  kBarSFull = 7,    // +S buffer
+  kBarSFree = 9,    // +S buffer
+  kBarPFull = 11,   // +P buffer
+  kBarPFree = 13,   // +P buffer
+  kBarOFull = 15,   // one completion per PV
+  kBarDone = 16,
+  kNumBars = 17
 };
 
 // 2^x by the MUFU instruction (ex2.approx.ftz: 2^-22 relative error, -inf -> +0).
@@ -203,7 +205,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(bar + 8 * (kBarSFull + b), 1);
       mbar_init(bar + 8 * (kBarSFree + b), 8);
     }
-    mbar_init(bar + 8 * kBarPFull, 8);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(bar + 8 * (kBarPFull + b), 8);
+      mbar_init(bar + 8 * (kBarPFree + b), 1);
+    }
     mbar_init(bar + 8 * kBarOFull, 1);
     mbar_init(bar + 8 * kBarDone, 1);
     fence_mbar_init();
@@ -309,17 +314,19 @@ __global__ void __launch_bounds__(kThreads, 1)
         fence_proxy_async_smem();
         __syncwarp();
       }
-      if (!wait_or_flag(bar + 8 * kBarPFull, j & 1, failed)) break;
+      if (!wait_or_flag(bar + 8 * (kBarPFull + (j & 1)), (j >> 1) & 1, failed)) break;
       tc::fence_after_sync();
       if (lane == 0) {
+        const uint32_t pbuf = base + L::oP + (j & 1) * L::kTileP;
 #pragma unroll
         for (int kk = 0; kk < kBN / 16; ++kk) {
-          const uint64_t a = tc::smem_desc_sw128(base + L::oP + (kk >> 2) * L::kPanel + (kk & 3) * 32, 16, 1024);
+          const uint64_t a = tc::smem_desc_sw128(pbuf + (kk >> 2) * L::kPanel + (kk & 3) * 32, 16, 1024);
           const uint64_t b = tc::smem_desc_sw128(base + L::oV + s * L::kTileKV + kk * 2048, L::kPanel, 1024);
           tc::mma_ss(tmem + kColO, a, b, idesc_pv, j > 0 || kk > 0);
         }
         if (split) {
-          const uint32_t plo = base + (L::kPloInK ? L::oK + s * L::kTileKV : L::oPloSep);
+          const uint32_t plo =
+              base + (L::kPloInK ? L::oK + s * L::kTileKV : L::oPloSep + (j & 1) * L::kTileP);
 #pragma unroll
           for (int kk = 0; kk < kBN / 16; ++kk) {
             const uint64_t a = tc::smem_desc_sw128(plo + (kk >> 2) * L::kPanel + (kk & 3) * 32, 16, 1024);
@@ -327,6 +334,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             tc::mma_ss(tmem + kColO, a, b, idesc_pv, true);
           }
         }
+        tc::commit(bar + 8 * (kBarPFree + (j & 1)));
         tc::commit(bar + 8 * kBarOFull);
         tc::commit(bar + 8 * (kBarKVEmpty + s));
       }
@@ -345,10 +353,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int pos = qpos0 + qi;
     const int vis = row_valid ? (p.causal ? min(ceil16, pos + 1) : ceil16) : 0;
     const float c = p.scale_log2;
-    float* xchg = reinterpret_cast<float*>(sbase + L::oX);  // [parity][half][128] maxima, then [half][128] sums
+    float* xchg = reinterpret_cast<float*>(sbase + L::oX);  // [half][128]: row maxima per tile, then sums
     float m_ref = -INFINITY;
     float l = 0.f;
-    char* ph = sbase + L::oP + half * L::kPanel + m * 128;
     // After a failed (timed-out) wait the loop keeps its shape with the waits
     // skipped, so both warpgroups still meet at every named barrier.
     for (int j = 0; j < ntiles; ++j) {
@@ -393,14 +400,18 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         cm = 1.f;
       }
-      // Row max over both halves.
-      xchg[(j & 1) * 256 + half * 128 + m] = mloc;
+      // Row max over both halves (second barrier: both reads done before the
+      // next tile's writes).
+      xchg[half * 128 + m] = mloc;
       named_bar_sync(1 + q4, 64);
-      const float mb = fmaxf(mloc, xchg[(j & 1) * 256 + (1 - half) * 128 + m]);
+      const float mb = fmaxf(mloc, xchg[(1 - half) * 128 + m]);
+      named_bar_sync(1 + q4, 64);
       const bool need = mb > m_ref + kLazyThreshold;
-      // PV(j-1) must be complete: it reads the P buffers and accumulates O.
-      if (j > 0) wait_or_flag(bar + 8 * kBarOFull, (j - 1) & 1, failed);
-      tc::fence_after_sync();
+      // P buffer j % 2 is free once PV(j-2) has completed. Waiting for it
+      // first also makes the O-stability wait below unambiguous: with PV(j-2)
+      // done, the one-completion-per-PV barrier is at most one phase from
+      // PV(j-1).
+      if (j >= 2) wait_or_flag(bar + 8 * (kBarPFree + (j & 1)), ((j >> 1) - 1) & 1, failed);
       float factor = 1.f;
       if (need) {
         factor = fast_exp2(m_ref - mb);  // 0 while m_ref is -inf
@@ -408,7 +419,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         m_ref = mb;
       }
       if (j > 0 && __any_sync(kFullMask, need)) {
-        // warp-collective: rows that keep their reference max scale by 1
+        // O must be stable: PV(j-1) complete. Warp-collective; rows that keep
+        // their reference max scale by 1.
+        wait_or_flag(bar + 8 * kBarOFull, (j - 1) & 1, failed);
+        tc::fence_after_sync();
 #pragma unroll
         for (int cc = 0; cc < D / 64; ++cc) {
           float o[32];
@@ -422,7 +436,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc::tmem_wait_st();
       }
       const float neg_m = m_ref == -INFINITY ? 0.f : -m_ref;
-      char* pl = sbase + (L::kPloInK ? L::oK + (j & 1) * L::kTileKV : L::oPloSep) + half * L::kPanel + m * 128;
+      char* ph = sbase + L::oP + (j & 1) * L::kTileP + half * L::kPanel + m * 128;
+      char* pl = sbase + (L::kPloInK ? L::oK + (j & 1) * L::kTileKV : L::oPloSep + (j & 1) * L::kTileP) +
+                 half * L::kPanel + m * 128;
 #pragma unroll
       for (int ch = 0; ch < 8; ++ch) {
         uint32_t hi[4], lo[4];
@@ -444,15 +460,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       fence_proxy_async_smem();
       tc::fence_before_sync();
       __syncwarp();
-      if (lane == 0) mbar_arrive(bar + 8 * kBarPFull);
+      if (lane == 0) mbar_arrive(bar + 8 * (kBarPFull + (j & 1)));
     }
     // ------------------------------------------------------------ epilogue
     wait_or_flag(bar + 8 * kBarOFull, (ntiles - 1) & 1, failed);
     tc::fence_after_sync();
-    xchg[512 + half * 128 + m] = l;
+    xchg[half * 128 + m] = l;
     named_bar_sync(1 + q4, 64);
     if (!__any_sync(kFullMask, failed)) {  // warp-uniform: tcgen05.ld is warp-collective
-      const float l_tot = l + xchg[512 + (1 - half) * 128 + m];
+      const float l_tot = l + xchg[(1 - half) * 128 + m];
       const float inv = 1.f / l_tot;
       T* op = reinterpret_cast<T*>(p.out) + (int64_t)(q_start + qi) * p.o_st + (int64_t)(kvh * G + gh) * p.o_sh +
               half * (D / 2);
