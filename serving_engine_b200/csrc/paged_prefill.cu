@@ -10,11 +10,13 @@
 // MMA rows pack (query, head) pairs of the GQA group, row m = query (m / G),
 // head (m % G), so each K/V tile is read once for the whole group:
 //   warp 0     TMA producer: the Q tile once, then K and V tiles of 128 keys
-//              (8 paged blocks, gathered through the block table) into a
-//              2-stage ring of 128B-swizzled K-major panels;
-//   warp 1     owns TMEM (512 columns: S double buffer at 0 and 128, O at 256)
-//              and issues the MMAs from one thread: S = Q K^T (M=128, N=128,
-//              K=head_dim) and O += P V (M=128, N=head_dim, K=128 keys);
+//              (8 paged blocks, gathered through the block table) into 2-stage
+//              rings of 128B-swizzled K-major panels; K runs two tiles ahead of
+//              V, matching the order the MMAs consume them;
+//   warp 1     owns TMEM (512 columns: three S buffers at 0/128/256, O at 384)
+//              and issues the MMAs from one thread: S(j+2) = Q K(j+2)^T is
+//              issued before O += P(j) V(j), so two score tiles are always in
+//              flight while the softmax works on a third;
 //   warps 2-9  two softmax warpgroups; a thread owns half of one tile row
 //              (TMEM lane): read its 64 scores, mask boundary tiles, agree on
 //              the row max with its partner thread through shared memory,
@@ -43,10 +45,11 @@ constexpr unsigned kFullMask = 0xffffffffu;
 constexpr int kBM = 128;        // MMA rows per CTA
 constexpr int kBN = 128;        // keys per KV tile
 constexpr int kThreads = 320;   // producer, MMA, 8 softmax warps (2 warpgroups)
-constexpr int kRing = 2;        // K/V ring depth
+constexpr int kRing = 2;        // K and V ring depths
+constexpr int kSBufs = 3;       // score buffers in TMEM
 constexpr int kTmemCols = 512;
-constexpr int kColS = 0;        // S buffers at columns 0 and 128
-constexpr int kColO = 256;      // O accumulator
+constexpr int kColS = 0;        // S buffers at columns 0, 128, 256
+constexpr int kColO = 384;      // O accumulator
 constexpr float kLazyThreshold = 8.0f;
 constexpr int kSplitBelow = 256;
 
@@ -83,13 +86,9 @@ struct PrefillLayout {
   static constexpr int oQ = 0;
   static constexpr int oK = oQ + kTileQ;
   static constexpr int oV = oK + kRing * kTileKV;
-  static constexpr int oP = oV + kRing * kTileKV;  // two P buffers (tiles j even / odd)
-  // P's 16-bit remainder (split tiles): in the K stage of the same tile when a
-  // K tile can hold it (S of that tile has consumed K by then), else its own
-  // pair of buffers.
-  static constexpr bool kPloInK = kTileKV >= kTileP;
-  static constexpr int oPloSep = oP + 2 * kTileP;
-  static constexpr int oBar = oPloSep + (kPloInK ? 0 : 2 * kTileP);
+  static constexpr int oP = oV + kRing * kTileKV;
+  static constexpr int oPlo = oP + kTileP;  // P's 16-bit remainder (split tiles)
+  static constexpr int oBar = oPlo + kTileP;
   static constexpr int oX = oBar + 256;  // row max / sum exchange between the two softmax warpgroups
   static constexpr int kBytes = oX + 2 * 128 * 4;
 };
@@ -99,14 +98,14 @@ enum {
   kBarQ = 0,
   kBarKFull = 1,    // +stage
   kBarVFull = 3,    // +stage
-  kBarKVEmpty = 5,  // +stage
-  kBarSFull = 7,    // +S buffer
-  kBarSFree = 9,    // +S buffer
-  kBarPFull = 11,   // +P buffer
-  kBarPFree = 13,   // +P buffer
-  kBarOFull = 15,   // one completion per PV
-  kBarDone = 16,
-  kNumBars = 17
+  kBarKEmpty = 5,   // +stage: S of the tile has consumed K
+  kBarVEmpty = 7,   // +stage: PV of the tile has consumed V
+  kBarSFull = 9,    // +S buffer (3)
+  kBarSFree = 12,   // +S buffer (3)
+  kBarPFull = 15,
+  kBarPFree = 16,   // one completion per PV (P buffer free, O stable)
+  kBarDone = 17,
+  kNumBars = 18
 };
 
 // 2^x by the MUFU instruction (ex2.approx.ftz: 2^-22 relative error, -inf -> +0).
@@ -199,17 +198,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int s = 0; s < kRing; ++s) {
       mbar_init(bar + 8 * (kBarKFull + s), 1);
       mbar_init(bar + 8 * (kBarVFull + s), 1);
-      mbar_init(bar + 8 * (kBarKVEmpty + s), 1);
+      mbar_init(bar + 8 * (kBarKEmpty + s), 1);
+      mbar_init(bar + 8 * (kBarVEmpty + s), 1);
     }
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < kSBufs; ++b) {
       mbar_init(bar + 8 * (kBarSFull + b), 1);
       mbar_init(bar + 8 * (kBarSFree + b), 8);
     }
-    for (int b = 0; b < 2; ++b) {
-      mbar_init(bar + 8 * (kBarPFull + b), 8);
-      mbar_init(bar + 8 * (kBarPFree + b), 1);
-    }
-    mbar_init(bar + 8 * kBarOFull, 1);
+    mbar_init(bar + 8 * kBarPFull, 8);
+    mbar_init(bar + 8 * kBarPFree, 1);
     mbar_init(bar + 8 * kBarDone, 1);
     fence_mbar_init();
   }
@@ -235,11 +232,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         tma_load_3d(base + L::oQ + pn * L::kPanel, &tmap_q, pn * 64, kvh * G, q_start + i0, bar + 8 * kBarQ);
     }
     const int32_t* bt = p.block_table + (int64_t)row * p.bt_stride;
-    int issued = 0;
-    for (int j = 0; j < ntiles; ++j) {
+    // Load K (is_v = 0) or V (is_v = 1) of tile j into stage j % 2.
+    auto load = [&](int j, int is_v) -> bool {
       const int s = j & 1;
       const int u = j >> 1;
-      if (u >= 1 && !wait_or_flag(bar + 8 * (kBarKVEmpty + s), (u - 1) & 1, failed)) break;
+      if (u >= 1 && !wait_or_flag(bar + 8 * ((is_v ? kBarVEmpty : kBarKEmpty) + s), (u - 1) & 1, failed))
+        return false;
       const int nb = min(8, nblk - 8 * j);
       int bid = 0;
       if (lane < nb) {
@@ -249,27 +247,30 @@ __global__ void __launch_bounds__(kThreads, 1)
           bid = 0;  // read a real block instead; the row's result is flagged as invalid
         }
       }
-      if (lane == 0) {
-        mbar_arrive_expect_tx(bar + 8 * (kBarKFull + s), nb * L::kPanels * 2048);
-        mbar_arrive_expect_tx(bar + 8 * (kBarVFull + s), nb * L::kPanels * 2048);
-      }
+      const uint32_t fb = bar + 8 * ((is_v ? kBarVFull : kBarKFull) + s);
+      if (lane == 0) mbar_arrive_expect_tx(fb, nb * L::kPanels * 2048);
       __syncwarp();
       if (lane < nb) {
+        const uint32_t dst = base + (is_v ? L::oV : L::oK) + s * L::kTileKV + lane * 2048;
 #pragma unroll
-        for (int pn = 0; pn < L::kPanels; ++pn) {
-          tma_load_3d(base + L::oK + s * L::kTileKV + pn * L::kPanel + lane * 2048, &tmap_k, pn * 64, kvh, bid * 16,
-                      bar + 8 * (kBarKFull + s));
-          tma_load_3d(base + L::oV + s * L::kTileKV + pn * L::kPanel + lane * 2048, &tmap_v, pn * 64, kvh, bid * 16,
-                      bar + 8 * (kBarVFull + s));
-        }
+        for (int pn = 0; pn < L::kPanels; ++pn)
+          tma_load_3d(dst + pn * L::kPanel, is_v ? &tmap_v : &tmap_k, pn * 64, kvh, bid * 16, fb);
       }
-      ++issued;
+      return true;
+    };
+    // Consumption order of the MMA warp: K(0), K(1), then per tile j K(j+2), V(j).
+    int k_issued = 0, v_issued = 0;
+    for (int j = 0; j < min(2, ntiles); ++j)
+      if (load(j, 0)) ++k_issued;
+    for (int j = 0; j < ntiles && !failed; ++j) {
+      if (load(j, 1)) ++v_issued;
+      if (j + 2 < ntiles && load(j + 2, 0)) ++k_issued;
     }
-    // Leave no copy in flight: the last tiles' loads must have landed.
-    for (int j = max(0, issued - kRing); j < issued; ++j) {
+    // Leave no copy in flight: the last loads must have landed.
+    for (int j = max(0, k_issued - kRing); j < k_issued; ++j)
       mbar_wait_bounded(bar + 8 * (kBarKFull + (j & 1)), (j >> 1) & 1, 1u << 16);
+    for (int j = max(0, v_issued - kRing); j < v_issued; ++j)
       mbar_wait_bounded(bar + 8 * (kBarVFull + (j & 1)), (j >> 1) & 1, 1u << 16);
-    }
   } else if (warp == 1) {
     // ---------------------------------------------------------------- MMA
     constexpr uint32_t idesc_qk = tc::idesc_f16(kBf16, false, kBM, kBN);
@@ -277,25 +278,27 @@ __global__ void __launch_bounds__(kThreads, 1)
     wait_or_flag(bar + 8 * kBarQ, 0, failed);
     auto issue_s = [&](int j) {
       const int s = j & 1;
-      const int u = j >> 1;
-      if (!wait_or_flag(bar + 8 * (kBarKFull + s), u & 1, failed)) return;
-      if (u >= 1 && !wait_or_flag(bar + 8 * (kBarSFree + s), (u - 1) & 1, failed)) return;
+      const int b = j % kSBufs;
+      const int u = j / kSBufs;
+      if (!wait_or_flag(bar + 8 * (kBarKFull + s), (j >> 1) & 1, failed)) return;
+      if (u >= 1 && !wait_or_flag(bar + 8 * (kBarSFree + b), (u - 1) & 1, failed)) return;
       tc::fence_after_sync();
       if (lane == 0) {
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint64_t a = tc::smem_desc_sw128(base + L::oQ + (kk >> 2) * L::kPanel + (kk & 3) * 32, 16, 1024);
-          const uint64_t b =
+          const uint64_t bd =
               tc::smem_desc_sw128(base + L::oK + s * L::kTileKV + (kk >> 2) * L::kPanel + (kk & 3) * 32, 16, 1024);
-          tc::mma_ss(tmem + kColS + s * kBN, a, b, idesc_qk, kk > 0);
+          tc::mma_ss(tmem + kColS + b * kBN, a, bd, idesc_qk, kk > 0);
         }
-        tc::commit(bar + 8 * (kBarSFull + s));
+        tc::commit(bar + 8 * (kBarSFull + b));
+        tc::commit(bar + 8 * (kBarKEmpty + s));
       }
       __syncwarp();
     };
-    if (!failed) issue_s(0);
+    for (int j = 0; j < min(2, ntiles) && !failed; ++j) issue_s(j);
     for (int j = 0; j < ntiles && !failed; ++j) {
-      if (j + 1 < ntiles) issue_s(j + 1);
+      if (j + 2 < ntiles) issue_s(j + 2);
       if (failed) break;
       const int s = j & 1;
       if (!wait_or_flag(bar + 8 * (kBarVFull + s), (j >> 1) & 1, failed)) break;
@@ -314,29 +317,25 @@ __global__ void __launch_bounds__(kThreads, 1)
         fence_proxy_async_smem();
         __syncwarp();
       }
-      if (!wait_or_flag(bar + 8 * (kBarPFull + (j & 1)), (j >> 1) & 1, failed)) break;
+      if (!wait_or_flag(bar + 8 * kBarPFull, j & 1, failed)) break;
       tc::fence_after_sync();
       if (lane == 0) {
-        const uint32_t pbuf = base + L::oP + (j & 1) * L::kTileP;
 #pragma unroll
         for (int kk = 0; kk < kBN / 16; ++kk) {
-          const uint64_t a = tc::smem_desc_sw128(pbuf + (kk >> 2) * L::kPanel + (kk & 3) * 32, 16, 1024);
-          const uint64_t b = tc::smem_desc_sw128(base + L::oV + s * L::kTileKV + kk * 2048, L::kPanel, 1024);
-          tc::mma_ss(tmem + kColO, a, b, idesc_pv, j > 0 || kk > 0);
+          const uint64_t a = tc::smem_desc_sw128(base + L::oP + (kk >> 2) * L::kPanel + (kk & 3) * 32, 16, 1024);
+          const uint64_t bd = tc::smem_desc_sw128(base + L::oV + s * L::kTileKV + kk * 2048, L::kPanel, 1024);
+          tc::mma_ss(tmem + kColO, a, bd, idesc_pv, j > 0 || kk > 0);
         }
         if (split) {
-          const uint32_t plo =
-              base + (L::kPloInK ? L::oK + s * L::kTileKV : L::oPloSep + (j & 1) * L::kTileP);
 #pragma unroll
           for (int kk = 0; kk < kBN / 16; ++kk) {
-            const uint64_t a = tc::smem_desc_sw128(plo + (kk >> 2) * L::kPanel + (kk & 3) * 32, 16, 1024);
-            const uint64_t b = tc::smem_desc_sw128(base + L::oV + s * L::kTileKV + kk * 2048, L::kPanel, 1024);
-            tc::mma_ss(tmem + kColO, a, b, idesc_pv, true);
+            const uint64_t a = tc::smem_desc_sw128(base + L::oPlo + (kk >> 2) * L::kPanel + (kk & 3) * 32, 16, 1024);
+            const uint64_t bd = tc::smem_desc_sw128(base + L::oV + s * L::kTileKV + kk * 2048, L::kPanel, 1024);
+            tc::mma_ss(tmem + kColO, a, bd, idesc_pv, true);
           }
         }
-        tc::commit(bar + 8 * (kBarPFree + (j & 1)));
-        tc::commit(bar + 8 * kBarOFull);
-        tc::commit(bar + 8 * (kBarKVEmpty + s));
+        tc::commit(bar + 8 * kBarPFree);
+        tc::commit(bar + 8 * (kBarVEmpty + s));
       }
       __syncwarp();
     }
@@ -346,8 +345,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_wait_bounded(bar + 8 * kBarDone, 0, 1u << 20);
   } else {
     // ------------------------------------------------------------ softmax
-    // Two warpgroups share each tile row: `half` 0 owns keys / O columns 0-63,
-    // half 1 owns 64-127. Warps w and w+4 see the same TMEM lanes (w % 4).
+    // Two warpgroups share each tile row: `half` 0 owns keys / O columns 0..D/2-1
+    // of its row, half 1 the rest. Warps w and w+4 see the same TMEM lanes (w % 4).
     const int half = (warp - 2) >> 2;
     const uint32_t taddr = tmem + ((uint32_t)(q4 * 32) << 16);
     const int pos = qpos0 + qi;
@@ -356,11 +355,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     float* xchg = reinterpret_cast<float*>(sbase + L::oX);  // [half][128]: row maxima per tile, then sums
     float m_ref = -INFINITY;
     float l = 0.f;
+    char* ph = sbase + L::oP + half * L::kPanel + m * 128;
+    char* pl = sbase + L::oPlo + half * L::kPanel + m * 128;
     // After a failed (timed-out) wait the loop keeps its shape with the waits
     // skipped, so both warpgroups still meet at every named barrier.
     for (int j = 0; j < ntiles; ++j) {
-      const int b = j & 1;
-      wait_or_flag(bar + 8 * (kBarSFull + b), (j >> 1) & 1, failed);
+      const int b = j % kSBufs;
+      wait_or_flag(bar + 8 * (kBarSFull + b), (j / kSBufs) & 1, failed);
       tc::fence_after_sync();
       float x[64];
       {
@@ -382,12 +383,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       // scaled here (keys past the row's visible range: -inf; zero-padded keys
       // of the last block: 0).
       const bool full = (j + 1) * kBN <= min_vis && (j + 1) * kBN <= k_len;
-      float mloc = -INFINITY, cm = c;
-      if (full) {
-#pragma unroll
-        for (int i = 0; i < 64; ++i) mloc = fmaxf(mloc, x[i]);
-        mloc *= c;
-      } else {
+      float cm = c;
+      if (!full) {
         const int kbase = j * kBN + half * 64;
 #pragma unroll
         for (int i = 0; i < 64; ++i) {
@@ -396,10 +393,18 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (key >= vis) v = -INFINITY;
           else if (key >= k_len) v = 0.f;
           x[i] = v;
-          mloc = fmaxf(mloc, v);
         }
         cm = 1.f;
       }
+      float mx[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) mx[i] = fmaxf(x[i], x[8 + i]);
+#pragma unroll
+      for (int i = 16; i < 64; i += 8)
+#pragma unroll
+        for (int k = 0; k < 8; ++k) mx[k] = fmaxf(mx[k], x[i + k]);
+      float mloc = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])), fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
+      mloc *= cm;
       // Row max over both halves (second barrier: both reads done before the
       // next tile's writes).
       xchg[half * 128 + m] = mloc;
@@ -407,22 +412,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float mb = fmaxf(mloc, xchg[(1 - half) * 128 + m]);
       named_bar_sync(1 + q4, 64);
       const bool need = mb > m_ref + kLazyThreshold;
-      // P buffer j % 2 is free once PV(j-2) has completed. Waiting for it
-      // first also makes the O-stability wait below unambiguous: with PV(j-2)
-      // done, the one-completion-per-PV barrier is at most one phase from
-      // PV(j-1).
-      if (j >= 2) wait_or_flag(bar + 8 * (kBarPFree + (j & 1)), ((j >> 1) - 1) & 1, failed);
       float factor = 1.f;
       if (need) {
         factor = fast_exp2(m_ref - mb);  // 0 while m_ref is -inf
         l *= factor;
         m_ref = mb;
       }
+      // PV(j-1) must be complete: it reads the P buffers and accumulates O.
+      if (j > 0) wait_or_flag(bar + 8 * kBarPFree, (j - 1) & 1, failed);
+      tc::fence_after_sync();
       if (j > 0 && __any_sync(kFullMask, need)) {
-        // O must be stable: PV(j-1) complete. Warp-collective; rows that keep
-        // their reference max scale by 1.
-        wait_or_flag(bar + 8 * kBarOFull, (j - 1) & 1, failed);
-        tc::fence_after_sync();
+        // warp-collective: rows that keep their reference max scale by 1
 #pragma unroll
         for (int cc = 0; cc < D / 64; ++cc) {
           float o[32];
@@ -436,9 +436,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc::tmem_wait_st();
       }
       const float neg_m = m_ref == -INFINITY ? 0.f : -m_ref;
-      char* ph = sbase + L::oP + (j & 1) * L::kTileP + half * L::kPanel + m * 128;
-      char* pl = sbase + (L::kPloInK ? L::oK + (j & 1) * L::kTileKV : L::oPloSep + (j & 1) * L::kTileP) +
-                 half * L::kPanel + m * 128;
+      float ls[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int ch = 0; ch < 8; ++ch) {
         uint32_t hi[4], lo[4];
@@ -446,7 +444,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int e = 0; e < 4; ++e) {
           const float a0 = fast_exp2(fmaf(x[8 * ch + 2 * e], cm, neg_m));
           const float a1 = fast_exp2(fmaf(x[8 * ch + 2 * e + 1], cm, neg_m));
-          l += a0 + a1;
+          ls[e] += a0 + a1;
           hi[e] = Mma<T>::pack(a0, a1);
           if (split) {
             const float2 f = Mma<T>::unpack(hi[e]);
@@ -457,13 +455,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         *reinterpret_cast<uint4*>(ph + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
         if (split) *reinterpret_cast<uint4*>(pl + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
       }
+      l += (ls[0] + ls[1]) + (ls[2] + ls[3]);
       fence_proxy_async_smem();
       tc::fence_before_sync();
       __syncwarp();
-      if (lane == 0) mbar_arrive(bar + 8 * (kBarPFull + (j & 1)));
+      if (lane == 0) mbar_arrive(bar + 8 * kBarPFull);
     }
     // ------------------------------------------------------------ epilogue
-    wait_or_flag(bar + 8 * kBarOFull, (ntiles - 1) & 1, failed);
+    wait_or_flag(bar + 8 * kBarPFree, (ntiles - 1) & 1, failed);
     tc::fence_after_sync();
     xchg[half * 128 + m] = l;
     named_bar_sync(1 + q4, 64);
