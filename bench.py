@@ -52,12 +52,13 @@ def parse_args():
     ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="decode", choices=["decode", "prefill"],
-                    help="decode: config 2 (the headline line); prefill: config 3")
+    ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "e2e"],
+                    help="decode: config 2 (the headline line); prefill: config 3; e2e: config 4")
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--batch", type=int, default=64)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer e2e leg (short profiling runs)")
+    ap.add_argument("--e2e-budget", type=int, default=8192, help="max_num_batched_tokens of the config-4 engine")
     return ap.parse_args()
 
 
@@ -417,6 +418,56 @@ def run_prefill_workload(args, device):
     }
 
 
+# ----------------------------------------------------------- config 4 end to end
+def run_e2e_workload(args, device):
+    """Config 4: random-init 16-layer Llama (hidden 2048, 32/8 heads, FFN 8192,
+    vocab 32000), bf16, 256 requests arriving at t=0 with lognormal prompts
+    (median 512, clipped to [32, 4096]) and 128 greedy tokens each, served with
+    continuous batching through the registered "paged|b200" attention."""
+    from serving_engine_b200 import ops
+    from serving_engine_b200.e2e import E2EEngine, config4_requests, random_llama
+
+    model = random_llama("config4", seed=args.seed, dtype=torch.bfloat16, device=device)
+    prompts = config4_requests(seed=args.seed)
+    max_new = 128
+    total_tokens = sum(len(p) + max_new for p in prompts)
+    num_blocks = int(total_tokens / 16 * 1.1) + 512
+    # warm-up: a few short requests through the same engine shape
+    warm = E2EEngine(model, num_blocks=2048, max_num_batched_tokens=args.e2e_budget, max_num_seqs=256)
+    for p in prompts[:8]:
+        warm.add_request(p[:64], 4)
+    warm.run()
+    del warm
+    torch.cuda.synchronize(device)
+    eng = E2EEngine(model, num_blocks=num_blocks, max_num_batched_tokens=args.e2e_budget, max_num_seqs=256)
+    for p in prompts:
+        eng.add_request(p, max_new)
+    launches0 = ops.LAUNCHES[0]
+    t0 = time.perf_counter()
+    eng.run()
+    torch.cuda.synchronize(device)
+    wall = time.perf_counter() - t0
+    ops.check_device_errors(device)
+    gen = sum(len(s.out) for s in eng.done)
+    dec = [st for st in eng.stats if st.kind == "decode"]
+    dec_tok = sum(st.new_tokens for st in dec)
+    dec_s = sum(st.seconds for st in dec)
+    return {
+        "metric": "end-to-end decode tokens/sec (config 4)", "value": round(gen / wall, 1), "unit": "tokens/s",
+        "n_gpus": 1, "steps": len(eng.stats), "warmup": 1, "ms_per_step": round(wall / len(eng.stats) * 1e3, 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (random-init weights, seeded random token ids)",
+        "config": {"workload": "config 4: 16-layer Llama 2048/32q/8kv/FFN 8192/vocab 32000, 256 requests, "
+                               "lognormal prompts (median 512, [32, 4096]), 128 greedy tokens each",
+                   "prompt_tokens": sum(len(p) for p in prompts), "generated_tokens": gen,
+                   "max_num_batched_tokens": args.e2e_budget, "max_num_seqs": 256},
+        "wall_s": round(wall, 3),
+        "decode_only": {"tokens_per_s": round(dec_tok / dec_s, 1) if dec_s else None, "steps": len(dec),
+                        "ms_per_step": round(dec_s / max(len(dec), 1) * 1e3, 3)},
+        "gpu_launches": ops.LAUNCHES[0] - launches0,
+    }
+
+
 def main():
     args = parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -436,6 +487,10 @@ def main():
     if args.workload == "prefill":
         if rank == 0:
             print(json.dumps(run_prefill_workload(args, device)), flush=True)
+        return
+    if args.workload == "e2e":
+        if rank == 0:
+            print(json.dumps(run_e2e_workload(args, device)), flush=True)
         return
     dist = None
     if world > 1:

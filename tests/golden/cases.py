@@ -66,3 +66,10 @@ def kv_append_inputs(dtype: torch.dtype):
     v_src = torch.randn(1, s, hkv, d, generator=gen).to(dtype)
     slots = torch.randperm(nb * 16, generator=gen)[:s]
     return kv, k_src, v_src, slots
+
+
+def e2e_prompts():
+    """(prompts, max_new_tokens) of the end-to-end greedy-parity fixture."""
+    gen = torch.Generator().manual_seed(31)
+    lens = [20, 37, 5, 64]
+    return [torch.randint(0, 1000, (n,), generator=gen).tolist() for n in lens], 12

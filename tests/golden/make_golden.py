@@ -179,6 +179,46 @@ def scheduler_trace(meta: dict) -> None:
     meta["scheduler_trace"] = steps
 
 
+def e2e_trace(meta: dict) -> None:
+    """Greedy tokens of the reference engine itself (LLMEngine + Scheduler +
+    BlockManager + ModelRunner.forward, eager paged attention, fp32, CPU) on a
+    seeded tiny random Llama, with chunked prefill forced by a small budget."""
+    from serving_engine.block import BLOCK_SIZE
+    from serving_engine.block_manager import BlockManager
+    from serving_engine.engine import LLMEngine
+    from serving_engine.model_runner import ModelRunner
+    from serving_engine.scheduler import Scheduler
+
+    from serving_engine_b200.e2e import random_llama
+    from tests.golden.cases import e2e_prompts
+
+    model = random_llama("tiny", seed=0)
+    cfg = model.config
+    runner = object.__new__(ModelRunner)
+    runner.device = "cpu"
+    runner.dtype = torch.float32
+    runner.attn_implementation = "paged|eager"
+    runner.model = model
+    runner.model.set_attn_implementation("paged|eager")
+    runner.block_size = BLOCK_SIZE
+    runner.num_gpu_blocks = 64
+    runner.tokenizer = None
+    runner.kv_cache = torch.zeros(cfg.num_hidden_layers, 2, 64, BLOCK_SIZE, cfg.num_key_value_heads, cfg.head_dim)
+    engine = object.__new__(LLMEngine)
+    engine.model_runner = runner
+    engine.block_manager = BlockManager(64, BLOCK_SIZE)
+    engine.scheduler = Scheduler(engine.block_manager, max_num_batched_tokens=32)
+    engine.requests = {}
+    prompts, max_new = e2e_prompts()
+    ids = [engine.add_request(prompt_token_ids=p, max_new_tokens=max_new, ignore_eos=True) for p in prompts]
+    steps = 0
+    while engine.scheduler.has_unfinished_requests():
+        engine.step()
+        steps += 1
+    meta["e2e_tiny_fp32"] = {"outputs": [engine.requests[r].output_token_ids for r in ids], "steps": steps,
+                             "max_num_batched_tokens": 32, "num_gpu_blocks": 64, "model": "tiny", "seed": 0}
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default=os.environ.get("SEB_REFERENCE", "/root/reference"))
@@ -189,6 +229,7 @@ def main() -> None:
     attention_cases(arrays, meta)
     kv_append_case(arrays, meta)
     scheduler_trace(meta)
+    e2e_trace(meta)
     import transformers
     meta["_generated_with"] = {"torch": torch.__version__, "transformers": transformers.__version__,
                                "numpy": np.__version__}
