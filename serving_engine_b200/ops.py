@@ -55,7 +55,9 @@ def err_word(dev: torch.device) -> torch.Tensor:
     idx = dev.index if dev.index is not None else torch.cuda.current_device()
     w = _err_words.get(idx)
     if w is None:
-        w = torch.zeros(1, dtype=torch.int32, device=torch.device("cuda", idx))
+        # a normal tensor even when first touched under torch.inference_mode
+        with torch.inference_mode(False):
+            w = torch.zeros(1, dtype=torch.int32, device=torch.device("cuda", idx))
         _err_words[idx] = w
     return w
 
@@ -77,7 +79,8 @@ def workspace(dev: torch.device, nbytes: int) -> torch.Tensor:
     idx = dev.index if dev.index is not None else torch.cuda.current_device()
     ws = _workspaces.get(idx)
     if ws is None or ws.numel() < nbytes:
-        ws = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=torch.device("cuda", idx))
+        with torch.inference_mode(False):
+            ws = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=torch.device("cuda", idx))
         _workspaces[idx] = ws
     return ws
 
