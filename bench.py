@@ -120,14 +120,30 @@ class ClockSampler:
 
 
 # --------------------------------------------------------------- our arm
+def shard_spec(batch: int, world: int, rank: int, seed: int, hq: int = 32, hkv: int = 8) -> dict:
+    """Rank `rank`'s share of the kv-head-sharded decode workload: a global batch
+    of batch*world sequences, of which this rank holds hkv/world kv heads (and
+    hq/world q heads) of every sequence, so per-rank work equals the 1-GPU work."""
+    if hkv % world or hq % world:
+        raise ValueError(f"{world} ranks must divide the {hkv} kv heads and {hq} q heads")
+    return {"batch": batch * world, "hq": hq // world, "hkv": hkv // world, "seed": seed * 1000 + rank}
+
+
+def max_over_ranks(dist, value: float, device) -> float:
+    """The largest value over all ranks (the job's time is its slowest rank's)."""
+    if dist is None:
+        return value
+    t = torch.tensor([value], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
 def shard_batch(args, rank: int, world: int, device):
     from serving_engine_b200 import workloads
 
-    if 8 % world or 32 % world:
-        raise SystemExit(f"--gpus {world} must divide the 8 kv heads")
-    b = workloads.decode_batch(args.batch * world, 1024, 8192, 32 // world, 8 // world, 128, torch.bfloat16,
-                               seed=args.seed * 1000 + rank, fill=str(device))
-    return b
+    sp = shard_spec(args.batch, world, rank, args.seed)
+    return workloads.decode_batch(sp["batch"], 1024, 8192, sp["hq"], sp["hkv"], 128, torch.bfloat16,
+                                  seed=sp["seed"], fill=str(device))
 
 
 def run_ours(args, rank, world, device, dist):
@@ -165,11 +181,9 @@ def run_ours(args, rank, world, device, dist):
     launches = ops.LAUNCHES[0] - launches0
     clocks = sampler.stop()
     ms_total = ev0.elapsed_time(ev1)
-    t = torch.tensor([ms_total], dtype=torch.float64, device=device)
+    ms_total_max = max_over_ranks(dist, ms_total, device)
     if dist is not None:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
         dist.barrier()
-    ms_total_max = float(t.item())
     ms_per_step = ms_total_max / args.steps
     agg_bytes = kv_bytes_rank * world
     value = agg_bytes / (ms_per_step * 1e-3) / 1e9
@@ -253,11 +267,7 @@ def run_e2e(args, b, device, dist, world):
     t0 = time.perf_counter()
     for _ in range(n):
         step()
-    dt = time.perf_counter() - t0
-    t = torch.tensor([dt], dtype=torch.float64, device=device)
-    if dist is not None:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    dt = float(t.item())
+    dt = max_over_ranks(dist, time.perf_counter() - t0, device)
     gbs = b.kv_bytes() * world * n / dt / 1e9
     return {"value": round(gbs, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
             "steps": n, "ms_per_step": round(dt / n * 1e3, 4),

@@ -1,0 +1,53 @@
+"""Host-side logic of the multi-GPU bench path, run as world_size-2 gloo ranks
+on CPU: kv-head sharding of the decode workload and max-over-ranks timing."""
+import os
+import socket
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+import bench
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        spec = bench.shard_spec(64, world, rank, seed=0)
+        slowest = bench.max_over_ranks(dist, 10.0 + rank, torch.device("cpu"))
+        q.put((rank, spec, slowest))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2])
+def test_shard_spec_and_max_over_ranks_gloo(world):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = sorted(q.get(timeout=120) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    assert [r[2] for r in results] == [10.0 + world - 1] * world  # every rank sees the slowest time
+    specs = [r[1] for r in results]
+    assert all(s["batch"] == 64 * world and s["hkv"] == 8 // world and s["hq"] == 32 // world for s in specs)
+    assert len({s["seed"] for s in specs}) == world  # ranks hold different data
+    # per-rank units equal the 1-GPU config: batch x kv heads
+    assert specs[0]["batch"] * specs[0]["hkv"] == 64 * 8
+
+
+def test_shard_spec_rejects_indivisible_heads():
+    with pytest.raises(ValueError):
+        bench.shard_spec(64, 3, 0, seed=0)
