@@ -52,8 +52,12 @@ def parse_args():
     ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "e2e"],
-                    help="decode: config 2 (the headline line); prefill: config 3; e2e: config 4")
+    ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "e2e", "tp"],
+                    help="decode: config 2 (the headline line); prefill: config 3; e2e: config 4; "
+                         "tp: config 5 (tensor-parallel decode)")
+    ap.add_argument("--tp-batch", type=int, default=256)
+    ap.add_argument("--tp-context", type=int, default=4096)
+    ap.add_argument("--no-graph", action="store_true", help="tp: run the decode step eagerly")
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--batch", type=int, default=64)
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -478,6 +482,56 @@ def run_e2e_workload(args, device):
     }
 
 
+# ---------------------------------------------------- config 5 tensor-parallel decode
+def run_tp_workload(args, rank, world, device, dist):
+    """Config 5: random-init Llama-3-8B shape (32 layers, 4096, 32/8 heads, D=128,
+    FFN 14336, vocab 128256), bf16, decode batch 256 at 4096 context over a
+    synthetic pre-filled KV pool; weights and pool sharded by kv head over the
+    ranks, NCCL all-reduce after o_proj and down_proj (64 per step)."""
+    from serving_engine_b200 import ops
+    from serving_engine_b200.tp_decode import LLAMA3_8B, TPLlamaDecoder
+
+    dec = TPLlamaDecoder(LLAMA3_8B, rank, world, device, batch=args.tp_batch, context=args.tp_context,
+                         seed=args.seed)
+    graph = not args.no_graph
+    if graph:
+        dec.capture(warmup=2)
+    for _ in range(max(args.warmup, 3)):
+        dec.step()
+    torch.cuda.synchronize(device)
+    if dist is not None:
+        dist.barrier()
+    stream = torch.cuda.current_stream(device)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    launches0 = ops.LAUNCHES[0]
+    ev0.record(stream)
+    for _ in range(args.steps):
+        dec.step()
+    ev1.record(stream)
+    torch.cuda.synchronize(device)
+    ops.check_device_errors(device)
+    ms = max_over_ranks(dist, ev0.elapsed_time(ev1), device) / args.steps
+    kv_bytes = dec.kv.numel() * 2 // LLAMA3_8B.layers * LLAMA3_8B.layers  # whole pool shard read per step
+    weight_bytes = sum(t.numel() * 2 for w in dec.layers for t in w.values()) + dec.lm_head.numel() * 2
+    per_gpu_bytes = kv_bytes + weight_bytes
+    dec.release()
+    res = {
+        "metric": "tensor-parallel decode tokens/sec (config 5)", "value": round(args.tp_batch / (ms * 1e-3), 1),
+        "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (random-init weights, random pre-filled KV)",
+        "config": {"workload": "config 5: Llama-3-8B shape, decode batch 256 at 4096 context",
+                   "batch": args.tp_batch, "context": args.tp_context, "parallelism": f"tp{world} (kv-head shard)",
+                   "cuda_graph": graph, "all_reduces_per_step": 2 * LLAMA3_8B.layers if world > 1 else 0},
+        "hbm_bytes_per_step_per_gpu": per_gpu_bytes,
+        "roofline": {"bound": "hbm", "achieved": round(per_gpu_bytes / (ms * 1e-3) / 1e9, 1), "unit": "GB/s",
+                     "peak": peaks()[0], "frac": round(per_gpu_bytes / (ms * 1e-3) / 1e9 / peaks()[0], 4),
+                     "note": "weights + KV shard read once per step per GPU"},
+        "gpu_launches_per_step": None if graph else (ops.LAUNCHES[0] - launches0) // args.steps,
+    }
+    return res
+
+
 def main():
     args = parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -511,7 +565,10 @@ def main():
         tdist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
         dist = tdist
     try:
-        result = run_ours(args, rank, world, device, dist)
+        if args.workload == "tp":
+            result = run_tp_workload(args, rank, world, device, dist)
+        else:
+            result = run_ours(args, rank, world, device, dist)
         if rank == 0:
             print(json.dumps(result), flush=True)
     finally:

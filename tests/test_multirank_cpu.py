@@ -51,3 +51,41 @@ def test_shard_spec_and_max_over_ranks_gloo(world):
 def test_shard_spec_rejects_indivisible_heads():
     with pytest.raises(ValueError):
         bench.shard_spec(64, 3, 0, seed=0)
+
+
+def _tp_mlp_worker(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from serving_engine_b200.tp_decode import TPConfig, TPLlamaDecoder
+
+        cfg = TPConfig(layers=1, hidden=64, heads=4, kv_heads=2, head_dim=16, ffn=96, vocab=50)
+        dec = TPLlamaDecoder(cfg, rank, world, torch.device("cpu"), batch=3, context=20, seed=5, fill_kv=False)
+        h = torch.randn(3, 64, generator=torch.Generator().manual_seed(0)).to(torch.bfloat16)
+        out = dec.mlp(h, dec.layers[0]).float()
+        q.put((rank, out))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_tp_mlp_shards_sum_to_full_mlp_gloo():
+    """Column-parallel gate/up + row-parallel down + all-reduce over 2 gloo ranks
+    equals the unsharded SwiGLU of the same seeded weights."""
+    from serving_engine_b200.tp_decode import TPConfig, TPLlamaDecoder
+
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_tp_mlp_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    outs = dict(q.get(timeout=120) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    cfg = TPConfig(layers=1, hidden=64, heads=4, kv_heads=2, head_dim=16, ffn=96, vocab=50)
+    full = TPLlamaDecoder(cfg, 0, 1, torch.device("cpu"), batch=3, context=20, seed=5, fill_kv=False)
+    h = torch.randn(3, 64, generator=torch.Generator().manual_seed(0)).to(torch.bfloat16)
+    ref = full.mlp(h, full.layers[0]).float()
+    torch.testing.assert_close(outs[0], ref, atol=2e-3, rtol=2e-2)
+    torch.testing.assert_close(outs[0], outs[1], atol=0, rtol=0)  # every rank holds the reduced sum
