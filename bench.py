@@ -57,7 +57,7 @@ def parse_args():
                          "tp: config 5 (tensor-parallel decode)")
     ap.add_argument("--tp-batch", type=int, default=256)
     ap.add_argument("--tp-context", type=int, default=4096)
-    ap.add_argument("--no-graph", action="store_true", help="tp: run the decode step eagerly")
+    ap.add_argument("--no-graph", action="store_true", help="tp / e2e: run decode steps eagerly")
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--batch", type=int, default=64)
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -453,7 +453,11 @@ def run_e2e_workload(args, device):
     warm.run()
     del warm
     torch.cuda.synchronize(device)
-    eng = E2EEngine(model, num_blocks=num_blocks, max_num_batched_tokens=args.e2e_budget, max_num_seqs=256)
+    graphs = not args.no_graph
+    eng = E2EEngine(model, num_blocks=num_blocks, max_num_batched_tokens=args.e2e_budget, max_num_seqs=256,
+                    use_graphs=graphs, max_context=4096 + max_new)
+    if graphs:
+        eng.capture_graphs()
     for p in prompts:
         eng.add_request(p, max_new)
     launches0 = ops.LAUNCHES[0]
@@ -474,7 +478,8 @@ def run_e2e_workload(args, device):
         "config": {"workload": "config 4: 16-layer Llama 2048/32q/8kv/FFN 8192/vocab 32000, 256 requests, "
                                "lognormal prompts (median 512, [32, 4096]), 128 greedy tokens each",
                    "prompt_tokens": sum(len(p) for p in prompts), "generated_tokens": gen,
-                   "max_num_batched_tokens": args.e2e_budget, "max_num_seqs": 256},
+                   "max_num_batched_tokens": args.e2e_budget, "max_num_seqs": 256,
+                   "cuda_graph_decode": graphs},
         "wall_s": round(wall, 3),
         "decode_only": {"tokens_per_s": round(dec_tok / dec_s, 1) if dec_s else None, "steps": len(dec),
                         "ms_per_step": round(dec_s / max(len(dec), 1) * 1e3, 3)},

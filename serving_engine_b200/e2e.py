@@ -21,6 +21,10 @@ parity on machines where the engine package is not installed:
 Unlike the reference, logits are computed for the last token of each row only
 (logits_to_keep), argmax runs on the device, and all next tokens come back in
 one device-to-host copy; preemption is not modelled (the pool is sized to fit).
+With use_graphs, decode-only steps replay a CUDA graph captured per padded
+batch-size bucket: the step's tokens, positions, slots, lengths and block
+tables go to fixed device buffers in two host-to-device copies, and pad rows
+attend over a reserved scratch block.
 """
 from __future__ import annotations
 
@@ -31,7 +35,7 @@ import numpy as np
 import torch
 
 from .kv_cache import PAGED_B200_ATTN_IMPL, PagedKVCache, register
-from .paged_attention import PackedMetadata
+from .paged_attention import DecodeMetadataBuffer, PackedMetadata
 
 BLOCK_SIZE = 16
 
@@ -46,6 +50,7 @@ class Seq:
     computed: int = 0
     prefilling: bool = True
     finished: bool = False
+    tab: np.ndarray | None = None  # block table as a fixed-width int32 row (graph path)
 
     @property
     def total_len(self) -> int:
@@ -63,8 +68,11 @@ class StepStats:
 class E2EEngine:
     """Continuous batching over `model` (a LlamaForCausalLM on a CUDA device)."""
 
+    GRAPH_BUCKETS = (1, 2, 4, 8, 16, 32, 64, 128, 256)
+
     def __init__(self, model, num_blocks: int, max_num_batched_tokens: int = 8192, max_num_seqs: int = 256,
-                 attn_implementation: str = PAGED_B200_ATTN_IMPL):
+                 attn_implementation: str = PAGED_B200_ATTN_IMPL, use_graphs: bool = False,
+                 max_context: int = 8192):
         if attn_implementation == PAGED_B200_ATTN_IMPL:
             register()
         model.set_attn_implementation(attn_implementation)
@@ -76,7 +84,13 @@ class E2EEngine:
         self.kv_cache = torch.zeros(cfg.num_hidden_layers, 2, num_blocks, BLOCK_SIZE, cfg.num_key_value_heads,
                                     head_dim, dtype=self.dtype, device=self.device)
         self.cache = PagedKVCache(self.kv_cache)
-        self.free = list(range(num_blocks))
+        self.use_graphs = use_graphs
+        self.width = -(-max_context // BLOCK_SIZE)
+        # the last block is reserved as the target of padded graph rows
+        self.scratch_block = num_blocks - 1 if use_graphs else None
+        self.free = list(range(num_blocks - 1 if use_graphs else num_blocks))
+        self.num_blocks = num_blocks
+        self.graphs: dict[int, dict] = {}
         self.max_tokens = max_num_batched_tokens
         self.max_seqs = max_num_seqs
         self.waiting: list[Seq] = []
@@ -92,6 +106,21 @@ class E2EEngine:
         return s.rid
 
     # ----------------------------------------------------------- scheduling
+    def _set_blocks(self, s: Seq, blocks) -> None:
+        s.table = list(blocks)
+        if self.use_graphs:
+            if len(s.table) > self.width:
+                raise ValueError(f"request of {s.total_len} tokens exceeds max_context {self.width * BLOCK_SIZE}")
+            s.tab = np.zeros(self.width, dtype=np.int32)
+            s.tab[:len(s.table)] = s.table
+
+    def _append_block(self, s: Seq, bid: int) -> None:
+        s.table.append(bid)
+        if self.use_graphs:
+            if len(s.table) > self.width:
+                raise ValueError(f"request exceeds max_context {self.width * BLOCK_SIZE}")
+            s.tab[len(s.table) - 1] = bid
+
     def _blocks_for(self, n_tokens: int) -> int:
         return -(-n_tokens // BLOCK_SIZE)
 
@@ -106,7 +135,7 @@ class E2EEngine:
             if len(s.table) * BLOCK_SIZE < s.total_len:
                 if not self.free:
                     continue
-                s.table.append(self.free.pop())
+                self._append_block(s, self.free.pop())
             rows.append((s, 0))
             budget -= 1
         for s in self.running:
@@ -122,7 +151,7 @@ class E2EEngine:
             if need > len(self.free):
                 break
             self.waiting.pop(0)
-            s.table = [self.free.pop() for _ in range(need)]
+            self._set_blocks(s, [self.free.pop() for _ in range(need)])
             self.running.append(s)
             chunk = min(s.total_len - s.computed, budget)
             rows.append((s, chunk))
@@ -139,6 +168,8 @@ class E2EEngine:
         if not rows:
             return 0
         t0 = time.perf_counter()
+        if self.graphs and all(c == 0 for _, c in rows) and len(rows) <= max(self.graphs):
+            return self._finish_step(rows, self._graph_decode(rows), t0, len(rows))
         toks, pos, slots = [], [], []
         q_lens, k_lens, q_pos = [], [], []
         for s, chunk in rows:
@@ -167,6 +198,11 @@ class E2EEngine:
                          past_key_values=None, use_cache=False, cache=self.cache, write_index=slot_t,
                          paged_metadata=md, logits_to_keep=last)
         next_tok = out.logits[0].argmax(dim=-1).tolist()
+        return self._finish_step(rows, next_tok, t0, len(toks))
+
+    def _finish_step(self, rows, next_tok, t0, n_tokens) -> int:
+        import time
+
         emitted = 0
         for (s, chunk), tok in zip(rows, next_tok):
             if chunk == 0:
@@ -185,11 +221,82 @@ class E2EEngine:
                 self.running.remove(s)
                 self.free.extend(s.table)
                 s.table = []
+                s.tab = None
                 self.done.append(s)
         kinds = {"decode" if c == 0 else "prefill" for _, c in rows}
-        self.stats.append(StepStats("mixed" if len(kinds) > 1 else kinds.pop(), len(toks), emitted,
+        self.stats.append(StepStats("mixed" if len(kinds) > 1 else kinds.pop(), n_tokens, emitted,
                                     time.perf_counter() - t0))
         return emitted
+
+    # ------------------------------------------------------------ CUDA graphs
+    def _graph_inputs(self, bucket: int) -> dict:
+        dev = self.device
+        st = {"host": torch.zeros(3, bucket, dtype=torch.int64).pin_memory()}
+        st["dev"] = st["host"].to(dev)
+        st["md"] = DecodeMetadataBuffer(bucket, self.width, dev)
+        st["last"] = torch.arange(bucket, device=dev)
+        return st
+
+    def _load_graph_inputs(self, st: dict, rows) -> None:
+        """Real rows first, then pad rows on the scratch block."""
+        b = len(rows)
+        bucket = st["last"].numel()
+        h = st["host"].numpy()
+        k_lens = np.ones(bucket, dtype=np.int32)
+        tables = np.zeros((bucket, self.width), dtype=np.int32)
+        tables[:, 0] = self.scratch_block
+        h[0, :] = 0
+        h[1, :] = 0
+        h[2, :] = self.scratch_block * BLOCK_SIZE
+        for i, (s, _) in enumerate(rows):
+            p = s.total_len - 1
+            h[0, i] = s.out[-1]
+            h[1, i] = p
+            h[2, i] = s.tab[p // BLOCK_SIZE] * BLOCK_SIZE + p % BLOCK_SIZE
+            k_lens[i] = s.total_len
+        if b:
+            tables[:b] = np.stack([s.tab for s, _ in rows])
+        st["dev"].copy_(st["host"], non_blocking=True)
+        st["md"].update(k_lens, tables)
+
+    def _run_graph_body(self, st: dict):
+        d = st["dev"]
+        out = self.model(input_ids=d[0].unsqueeze(0), position_ids=d[1].unsqueeze(0), attention_mask=None,
+                         past_key_values=None, use_cache=False, cache=self.cache, write_index=d[2],
+                         paged_metadata=st["md"].metadata, logits_to_keep=st["last"])
+        return out.logits[0].argmax(dim=-1)
+
+    @torch.inference_mode()
+    def capture_graphs(self, buckets=None) -> None:
+        """Capture one decode-step graph per batch-size bucket (largest first, so
+        the decode workspace is allocated at its largest size before capture)."""
+        if not self.use_graphs:
+            raise RuntimeError("engine built without use_graphs")
+        buckets = sorted(buckets or [b for b in self.GRAPH_BUCKETS if b <= self.max_seqs], reverse=True)
+        pool = torch.cuda.graph_pool_handle()
+        side = torch.cuda.Stream(device=self.device)
+        for bucket in buckets:
+            st = self._graph_inputs(bucket)
+            self._load_graph_inputs(st, [])
+            side.wait_stream(torch.cuda.current_stream(self.device))
+            with torch.cuda.stream(side):
+                for _ in range(2):
+                    self._run_graph_body(st)
+            torch.cuda.current_stream(self.device).wait_stream(side)
+            torch.cuda.synchronize(self.device)
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, pool=pool):
+                st["out"] = self._run_graph_body(st)
+            st["graph"] = g
+            self.graphs[bucket] = st
+        torch.cuda.synchronize(self.device)
+
+    def _graph_decode(self, rows) -> list:
+        bucket = min(b for b in self.graphs if b >= len(rows))
+        st = self.graphs[bucket]
+        self._load_graph_inputs(st, rows)
+        st["graph"].replay()
+        return st["out"][:len(rows)].tolist()
 
     def has_unfinished(self) -> bool:
         return bool(self.waiting or self.running)

@@ -24,6 +24,9 @@ _state = threading.local()
 LAUNCHES = [0]
 _err_words: dict[int, torch.Tensor] = {}
 _workspaces: dict[int, torch.Tensor] = {}
+# Workspaces outgrown by a larger call stay allocated: a captured CUDA graph may
+# still hold their address.
+_retired_workspaces: list[torch.Tensor] = []
 
 # SEB_DEBUG=1 checks the device error word after every op (one sync per op).
 DEBUG = os.environ.get("SEB_DEBUG", "0") not in ("", "0")
@@ -79,6 +82,8 @@ def workspace(dev: torch.device, nbytes: int) -> torch.Tensor:
     idx = dev.index if dev.index is not None else torch.cuda.current_device()
     ws = _workspaces.get(idx)
     if ws is None or ws.numel() < nbytes:
+        if ws is not None:
+            _retired_workspaces.append(ws)
         with torch.inference_mode(False):
             ws = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=torch.device("cuda", idx))
         _workspaces[idx] = ws

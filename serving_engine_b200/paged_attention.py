@@ -157,6 +157,47 @@ class PackedMetadata:
         }
 
 
+class DecodeMetadataBuffer:
+    """Fixed-shape step metadata for a decode-only batch of `rows` rows and a
+    block-table width `width`, resident in one device buffer whose address never
+    changes (what a captured CUDA graph reads). Layout as PackedMetadata with
+    q_len = 1 for every row: q_lens | k_lens | q_starts | q_pos_offsets |
+    block_table | item_row | decode tokens | decode rows (no prefill rows)."""
+
+    def __init__(self, rows: int, width: int, device):
+        self.rows, self.width = rows, width
+        n = 4 * rows + rows * width + 3 * rows
+        self.host = torch.zeros(n, dtype=torch.int32).pin_memory()
+        a = self.host.numpy()
+        ar = np.arange(rows, dtype=np.int32)
+        a[0:rows] = 1
+        a[2 * rows:3 * rows] = ar
+        o = 4 * rows + rows * width
+        a[o:o + rows] = ar          # item_row
+        a[o + rows:o + 2 * rows] = ar  # decode tokens
+        a[o + 2 * rows:o + 3 * rows] = ar  # decode rows
+        self.dev = self.host.to(device)
+        buf, r, w = self.dev, rows, width
+        self.metadata = {
+            "q_lens": buf[0:r], "k_lens": buf[r:2 * r], "q_starts": buf[2 * r:3 * r],
+            "q_pos_offsets": buf[3 * r:4 * r], "block_table": buf[4 * r:4 * r + r * w].view(r, w),
+            "block_table_row_stride": w, "total_query": r, "max_q_len": 1,
+            "item_row": buf[o:o + r], "max_block_id": -1, "max_k_len": w * ops.BLOCK_SIZE,
+            "decode_tokens": buf[o + r:o + 2 * r], "decode_rows": buf[o + 2 * r:o + 3 * r],
+            "prefill_rows": buf[o + 3 * r:o + 3 * r], "max_prefill_q_len": 0,
+        }
+
+    def update(self, k_lens: np.ndarray, tables: np.ndarray) -> None:
+        """Write this step's k_lens [rows] and block tables [rows, width] (host
+        side, pinned), then copy the buffer to the device asynchronously."""
+        r, w = self.rows, self.width
+        a = self.host.numpy()
+        a[r:2 * r] = k_lens
+        a[3 * r:4 * r] = k_lens - 1
+        a[4 * r:4 * r + r * w] = tables.reshape(-1)
+        self.dev.copy_(self.host, non_blocking=True)
+
+
 def metadata_from_lists(q_lens, k_lens, q_starts, q_pos_offsets, tables, device="cuda") -> dict:
     """The metadata dict from per-row host lists (one packed int32 H2D copy)."""
     return PackedMetadata(q_lens, k_lens, q_starts, q_pos_offsets, tables).upload(device)

@@ -15,10 +15,15 @@ from tests.golden.cases import e2e_prompts
 pytestmark = pytest.mark.gpu
 
 
-def test_greedy_tokens_match_reference_engine(golden_meta):
+@pytest.mark.parametrize("graphs", [False, True])
+def test_greedy_tokens_match_reference_engine(golden_meta, graphs):
+    """Also with the decode steps replayed from captured CUDA graphs."""
     g = golden_meta["e2e_tiny_fp32"]
     model = random_llama("tiny", seed=g["seed"], dtype=torch.float32, device="cuda")
-    eng = E2EEngine(model, num_blocks=g["num_gpu_blocks"], max_num_batched_tokens=g["max_num_batched_tokens"])
+    eng = E2EEngine(model, num_blocks=g["num_gpu_blocks"] + (1 if graphs else 0),
+                    max_num_batched_tokens=g["max_num_batched_tokens"], use_graphs=graphs, max_context=256)
+    if graphs:
+        eng.capture_graphs()
     prompts, max_new = e2e_prompts()
     rids = [eng.add_request(p, max_new) for p in prompts]
     eng.run()
@@ -26,6 +31,8 @@ def test_greedy_tokens_match_reference_engine(golden_meta):
     outs = {s.rid: s.out for s in eng.done}
     assert [outs[r] for r in rids] == g["outputs"]
     assert any(st.kind == "mixed" for st in eng.stats) or any(st.kind == "prefill" for st in eng.stats)
+    if graphs:
+        assert any(st.kind == "decode" for st in eng.stats)
 
 
 def test_bf16_engine_runs_chunked_and_mixed_steps():
