@@ -233,7 +233,7 @@ def run_ours(args, rank, world, device, dist):
         "frac": round(per_rank_gbs / hbm, 4),
         "peak_source": f"{src} (MEASURED_PEAKS.json hbm_gbs)" if src == "measured" else "fallback 6.65 TB/s",
         "frac_of_nominal_8000": round(per_rank_gbs / 8000.0, 4),
-        "kernel": "decode_mma_kernel + decode_combine_kernel (one paged_flash_attention call)",
+        "kernel": "decode_mma_kernel (split-K with in-kernel merge; one paged_flash_attention call)",
         "traffic": traffic,
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

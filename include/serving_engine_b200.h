@@ -115,7 +115,8 @@ SEB_API int seb_copy_blocks(void* kv_cache, int64_t num_layers, int64_t layer_st
  *
  * seb_paged_decode is the split-K decode kernel: one warp per
  * (query item, kv head, split of blocks_per_split blocks) with all query heads
- * of the GQA group packed on one tensor-core tile, followed by a combine pass.
+ * of the GQA group packed on one tensor-core tile; the last warp to finish a
+ * split of an (item, kv head) merges the splits in the same launch.
  * It is correct for any query (decode or prefill rows alike) and is the fast
  * path for q_len = 1 rows.
  *   item_query[i]: token index of item i (NULL: item i is token i); tokens
@@ -123,6 +124,10 @@ SEB_API int seb_copy_blocks(void* kv_cache, int64_t num_layers, int64_t layer_st
  *   item_row[i]:   its row (NULL: found by binary search over q_starts).
  *   blocks_per_split <= 0 picks a default.
  * workspace: at least seb_paged_decode_workspace_size(...) bytes, 16-byte aligned.
+ *   Nothing in it needs to start at zero: its last bytes hold one arrival
+ *   counter per (item, kv head), which the call clears on its stream
+ *   (cudaMemsetAsync, capturable in a CUDA graph) before the launch. Calls that
+ *   overlap on the GPU must not share a workspace.
  */
 SEB_API int64_t seb_paged_decode_workspace_size(int32_t num_items, int32_t num_q_heads,
                                         int32_t num_kv_heads, int32_t head_dim,

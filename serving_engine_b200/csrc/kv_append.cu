@@ -8,6 +8,7 @@
 //
 // Roofline: HBM, 2 * n_tokens * num_kv_heads * head_dim * elem bytes read and
 // the same written. Decode-sized calls (tens of tokens) are launch-latency bound.
+// One warp copies one token's K (or V) rows of every kv head.
 #include "seb_common.cuh"
 
 namespace seb {
@@ -29,34 +30,48 @@ struct AppendParams {
   int64_t num_slots;
   int64_t row_bytes;         // head_dim * elem
   int32_t num_kv_heads;
+  int32_t cph_shift;  // log2(row_bytes / VEC) when a power of two, else -1
   int32_t* err;
 };
 
-// Thread u copies chunk c of row (token t, plane kv, head h), with
-// u = ((t*2 + kv)*H + h)*chunks + c: consecutive threads write consecutive
-// bytes of one slot, so stores are fully coalesced.
+// One warp per (token t, plane kv): the token's num_kv_heads rows land
+// contiguously in its slot, so the warp's stores cover one contiguous range;
+// loads follow the source's token/head strides. Chunk c of the slot is head
+// c / chunks_per_head, offset c % chunks_per_head.
 template <int VEC>
 __global__ void __launch_bounds__(256) kv_append_kernel(AppendParams p) {
   using V = typename VecType<VEC>::T;
-  const int64_t chunks = p.row_bytes / VEC;
-  const int64_t per_token = 2 * (int64_t)p.num_kv_heads * chunks;
-  const int64_t total = p.n_tokens * per_token;
-  for (int64_t u = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; u < total;
-       u += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t t = u / per_token;
-    int64_t r = u - t * per_token;
-    const int kv = (int)(r / ((int64_t)p.num_kv_heads * chunks));
-    r -= (int64_t)kv * p.num_kv_heads * chunks;
-    const int64_t h = r / chunks;
-    const int64_t c = r - h * chunks;
-    const int64_t slot = __ldg(p.slots + t);
-    if (slot < 0 || slot >= p.num_slots) {
-      if (h == 0 && c == 0 && kv == 0) atomic_or_err(p.err, SEB_ERRBIT_SLOT);
-      continue;
+  const int64_t wid = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  const int64_t t = wid >> 1;
+  const int kv = (int)(wid & 1);
+  if (t >= p.n_tokens) return;
+  const int64_t slot = __ldg(p.slots + t);
+  if (slot < 0 || slot >= p.num_slots) {
+    if (lane == 0 && kv == 0) atomic_or_err(p.err, SEB_ERRBIT_SLOT);
+    return;
+  }
+  const int cph = (int)(p.row_bytes / VEC);  // chunks per head row
+  const int chunks = p.num_kv_heads * cph;
+  const char* src = p.src[kv] + t * p.st_tok[kv];
+  V* dst = reinterpret_cast<V*>(p.dst[kv] + slot * p.num_kv_heads * p.row_bytes);
+  const int64_t sth = p.st_head[kv];
+  constexpr int U = 4;
+  for (int c0 = lane; c0 < chunks; c0 += 32 * U) {
+    V v[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int c = c0 + 32 * u;
+      if (c < chunks) {
+        const int h = p.cph_shift >= 0 ? (c >> p.cph_shift) : c / cph;
+        v[u] = __ldg(reinterpret_cast<const V*>(src + h * sth) + (c - h * cph));
+      }
     }
-    const V* s = reinterpret_cast<const V*>(p.src[kv] + t * p.st_tok[kv] + h * p.st_head[kv]) + c;
-    V* d = reinterpret_cast<V*>(p.dst[kv] + (slot * p.num_kv_heads + h) * p.row_bytes) + c;
-    *d = __ldg(s);
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int c = c0 + 32 * u;
+      if (c < chunks) dst[c] = v[u];
+    }
   }
 }
 
@@ -107,10 +122,14 @@ extern "C" int seb_kv_append(const void* k_new, int64_t k_stride_token, int64_t 
   while (vec > es && !ok(vec)) vec >>= 1;
   SEB_CHECK_ARG(ok(vec), "seb_kv_append: pointers or strides not aligned to the element size");
 
-  const int64_t total = n_tokens * 2 * (int64_t)num_kv_heads * (p.row_bytes / vec);
-  int64_t blocks = (total + 255) / 256;
-  const int64_t cap = (int64_t)num_sms() * 16;
-  if (blocks > cap) blocks = cap;
+  const int64_t cph = p.row_bytes / vec;
+  p.cph_shift = -1;
+  for (int sh = 0; sh < 31; ++sh)
+    if ((1ll << sh) == cph) p.cph_shift = sh;
+  SEB_CHECK_ARG((int64_t)num_kv_heads * cph < (1ll << 30), "seb_kv_append: row too large");
+  const int64_t warps = n_tokens * 2;
+  const int64_t blocks = (warps + 7) / 8;
+  SEB_CHECK_ARG(blocks < (1ll << 31), "seb_kv_append: too many tokens");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   switch (vec) {
     case 16: kv_append_kernel<16><<<(unsigned)blocks, 256, 0, s>>>(p); break;

@@ -8,15 +8,17 @@
 // Design (one warp = one work item (query item, kv head, split)):
 //   * A split is <= 32 consecutive 16-token blocks of the row; the warp keeps the
 //     split's block ids in one register per lane and streams each block's K and
-//     V rows (16 + 16 rows of head_dim elements, one 1-D bulk async copy per lane)
-//     through a STAGES-deep shared-memory ring completed on mbarriers.
+//     V tiles (TMA tiled loads of 16 rows x 128-byte swizzled panels) through a
+//     STAGES-deep shared-memory ring completed on mbarriers.
 //   * All query heads of the GQA group share each KV tile: the 16 keys of a block
 //     are the M dimension of an m16n8k16 tensor-core tile and the (<= 8) heads of
 //     the group its N dimension, so S^T = K Q^T and O^T += V^T P^T each take
 //     head_dim/16 MMAs per block; P^T is moved from the accumulator layout to the
 //     operand layout with movmatrix. KV is read from HBM exactly once.
 //   * Online softmax in the log2 domain; per-split (m, l, O) go to a workspace
-//     and a combine pass merges splits. Items with one split write O/LSE directly.
+//     and the last warp to finish a split of an (item, kv head) merges them (an
+//     arrival counter per item and kv head, cleared by a small memset on the
+//     call's stream before the launch). Items with one split write O/LSE directly.
 //
 // fp32 (and any shape the tensor-core path does not cover) runs a CUDA-core
 // variant with the same work decomposition and workspace format.
@@ -65,6 +67,7 @@ struct DecodeParams {
   int64_t lse_st;
   float* ws_o;   // [items][hq][max_splits][D]
   float* ws_ml;  // [items][hq][max_splits][2]  (m in log2 units, l)
+  int32_t* counters;  // [items][hkv] splits finished; zero between calls
   int32_t* err;
 };
 
@@ -142,6 +145,124 @@ __device__ __forceinline__ int load_block_ids(const DecodeParams& p, const ItemI
     }
   }
   return bid;
+}
+
+// --------------------------------------------------------------------------
+// Split-K merge, run by the last warp to finish a split of an (item, kv head).
+// Up to 32 splits are merged for 4 query heads of the group at a time: lane s
+// loads split s's (m, l) of all 4 heads at once and turns them into weights
+// 2^(m_s - M); then each lane owns D/32 consecutive head dims and sums the
+// weighted partial O of every split, with the loads of 4 heads x KU splits in
+// flight together. Partials written by other SMs are read through L2
+// (ld.global.cg), never from a stale L1 line.
+// --------------------------------------------------------------------------
+template <typename T, int D>
+__device__ __forceinline__ void merge_heads(const DecodeParams& p, const ItemInfo& it, int64_t item, int qh0,
+                                            int nh, int lane) {
+  constexpr int HG = 4;                 // heads per pass
+  constexpr int VPL = D / 32;           // values per lane (2, 4 or 8)
+  constexpr int KU = D == 256 ? 2 : 4;  // splits per load batch
+  using Vec = typename std::conditional<VPL == 2, float2, float4>::type;
+  constexpr int NV = VPL == 2 ? 1 : VPL / 4;  // vector loads per (head, split)
+  constexpr int VW = VPL == 2 ? 2 : 4;        // floats per vector load
+  const int ns = it.n_splits;                 // >= 2
+  const float2* ml_base = reinterpret_cast<const float2*>(p.ws_ml) + (item * p.hq + qh0) * p.max_splits;
+
+  // (m, l) of splits lane, lane + 32, ... for every head; w0 = weight of split `lane`.
+  float w0[HG], m_use[HG], inv_l[HG], lse[HG];
+#pragma unroll
+  for (int h = 0; h < HG; ++h) {
+    const float2* ml = ml_base + (int64_t)h * p.max_splits;
+    const bool live = h < nh;
+    const float2 first = (live && lane < ns) ? __ldcg(ml + lane) : make_float2(-INFINITY, 0.f);
+    float mx = first.x;
+    for (int sidx = lane + 32; live && sidx < ns; sidx += 32) mx = fmaxf(mx, __ldcg(ml + sidx).x);
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(kFull, mx, off));
+    m_use[h] = (mx == -INFINITY) ? 0.f : mx;
+    w0[h] = (live && lane < ns) ? exp2f(first.x - m_use[h]) : 0.f;
+    float l = first.y * w0[h];
+    for (int sidx = lane + 32; live && sidx < ns; sidx += 32) {
+      const float2 v = __ldcg(ml + sidx);
+      l += v.y * exp2f(v.x - m_use[h]);
+    }
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) l += __shfl_xor_sync(kFull, l, off);
+    inv_l[h] = 1.f / l;
+    lse[h] = mx * kLn2 + logf(l);
+  }
+
+  float acc[HG][VPL];
+#pragma unroll
+  for (int h = 0; h < HG; ++h)
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) acc[h][i] = 0.f;
+  const float* wo0 = p.ws_o + (item * p.hq + qh0) * p.max_splits * D + lane * VPL;
+  const int64_t head_stride = (int64_t)p.max_splits * D;
+  for (int s0 = 0; s0 < ns; s0 += 32) {
+    float w[HG];
+#pragma unroll
+    for (int h = 0; h < HG; ++h) {
+      if (s0 == 0) {
+        w[h] = w0[h];
+      } else {
+        const bool live = h < nh && s0 + lane < ns;
+        w[h] = live ? exp2f(__ldcg(ml_base + (int64_t)h * p.max_splits + s0 + lane).x - m_use[h]) : 0.f;
+      }
+    }
+    const int cnt = min(32, ns - s0);
+    for (int k0 = 0; k0 < cnt; k0 += KU) {
+      Vec v[KU][HG][NV];
+#pragma unroll
+      for (int k = 0; k < KU; ++k)
+#pragma unroll
+        for (int h = 0; h < HG; ++h)
+#pragma unroll
+          for (int n = 0; n < NV; ++n) {
+            const float* src = wo0 + h * head_stride + (int64_t)(s0 + k0 + k) * D + n * 4;
+            if (h < nh && k0 + k < cnt) v[k][h][n] = __ldcg(reinterpret_cast<const Vec*>(src));
+            else v[k][h][n] = Vec{};
+          }
+#pragma unroll
+      for (int k = 0; k < KU; ++k)
+#pragma unroll
+        for (int h = 0; h < HG; ++h) {
+          const float wk = __shfl_sync(kFull, w[h], (k0 + k) & 31);
+#pragma unroll
+          for (int n = 0; n < NV; ++n) {
+            const float* f = reinterpret_cast<const float*>(&v[k][h][n]);
+#pragma unroll
+            for (int i = 0; i < VW; ++i) acc[h][n * VW + i] = fmaf(wk, f[i], acc[h][n * VW + i]);
+          }
+        }
+    }
+  }
+#pragma unroll
+  for (int h = 0; h < HG; ++h) {
+    if (h >= nh) break;
+    T* op = reinterpret_cast<T*>(p.out) + (int64_t)it.qtok * p.o_st + (int64_t)(qh0 + h) * p.o_sh + lane * VPL;
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) op[i] = Elem<T>::from_float(acc[h][i] * inv_l[h]);
+    if (lane == 0) p.lse[(int64_t)it.qtok * p.lse_st + qh0 + h] = lse[h];
+  }
+}
+
+// Called by every warp after writing its split's partials: the warp that
+// completes the (item, kv head) merges all splits of the group. The host clears
+// the counters before each launch.
+template <typename T, int D>
+__device__ __forceinline__ void finish_split(const DecodeParams& p, const ItemInfo& it, int64_t item, int kvh,
+                                             int lane) {
+  __threadfence();  // this lane's partials are visible device-wide before the arrival
+  __syncwarp();
+  int prev = 0;
+  int32_t* ctr = p.counters + item * p.hkv + kvh;
+  if (lane == 0) prev = atomicAdd(ctr, 1);
+  prev = __shfl_sync(kFull, prev, 0);
+  if (prev != it.n_splits - 1) return;
+  __threadfence();
+  for (int g0 = 0; g0 < p.group; g0 += 4)
+    merge_heads<T, D>(p, it, item, kvh * p.group + g0, min(4, p.group - g0), lane);
 }
 
 // --------------------------------------------------------------------------
@@ -410,10 +531,9 @@ __global__ void __launch_bounds__(WARPS * 32)
     __syncwarp();
     if (j + STAGES < nb) issue(j + STAGES);
   }
-  if (timed_out) {
-    if (lane == 0) atomic_or_err(p.err, SEB_ERRBIT_TIMEOUT);
-    return;
-  }
+  // A timed-out warp still reports its (invalid) partial so the split counter
+  // of its item stays consistent; the error word flags the call.
+  if (timed_out && lane == 0) atomic_or_err(p.err, SEB_ERRBIT_TIMEOUT);
 
   float l_tot[NTH][2];
 #pragma unroll
@@ -464,6 +584,7 @@ __global__ void __launch_bounds__(WARPS * 32)
           p.ws_ml[slot * 2 + 1] = l_tot[nt][h];
         }
       }
+    finish_split<T, D>(p, it, item, kvh, lane);
   }
 }
 
@@ -577,73 +698,8 @@ __global__ void __launch_bounds__(WARPS * 32) decode_simt_kernel(const DecodePar
         p.ws_ml[slot * 2 + 1] = l[gh];
       }
     }
+    finish_split<T, D>(p, it, item, kvh, lane);
   }
-}
-
-// --------------------------------------------------------------------------
-// Combine pass: one warp per (item, q head) with >= 2 splits. Lane s first
-// turns split s's (m, l) into its weight 2^(m_s - M); then each lane owns D/32
-// consecutive head dims and sums the weighted partial O of every split.
-// --------------------------------------------------------------------------
-template <typename T, int D>
-__global__ void __launch_bounds__(128) decode_combine_kernel(const DecodeParams p) {
-  constexpr int VPL = D / 32;  // values per lane (2, 4 or 8)
-  const int warp = threadIdx.x >> 5;
-  const int lane = threadIdx.x & 31;
-  const int64_t w = (int64_t)blockIdx.x * 4 + warp;
-  const int64_t item = w / p.hq;
-  const int qh = (int)(w % p.hq);
-  if (item >= p.num_items) return;
-  const ItemInfo it = item_info(p, (int)item);
-  if (!it.ok || it.n_splits <= 1) return;
-  const int64_t base = (item * p.hq + qh) * p.max_splits;
-  const float* ml = p.ws_ml + base * 2;
-  const int ns = it.n_splits;
-  float mx = -INFINITY;
-  for (int s = lane; s < ns; s += 32) mx = fmaxf(mx, ml[2 * s]);
-#pragma unroll
-  for (int off = 16; off >= 1; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(kFull, mx, off));
-  const float m_use = (mx == -INFINITY) ? 0.f : mx;
-  float lsum = 0.f;
-  for (int s = lane; s < ns; s += 32) lsum += ml[2 * s + 1] * exp2f(ml[2 * s] - m_use);
-#pragma unroll
-  for (int off = 16; off >= 1; off >>= 1) lsum += __shfl_xor_sync(kFull, lsum, off);
-
-  float acc[VPL];
-#pragma unroll
-  for (int i = 0; i < VPL; ++i) acc[i] = 0.f;
-  const float* wo = p.ws_o + base * D + lane * VPL;
-  for (int s0 = 0; s0 < ns; s0 += 32) {
-    const int sl = s0 + lane;
-    const float wl = sl < ns ? exp2f(ml[2 * sl] - m_use) : 0.f;
-    const int cnt = min(32, ns - s0);
-#pragma unroll 4
-    for (int k = 0; k < cnt; ++k) {
-      const float wk = __shfl_sync(kFull, wl, k);
-      const float* src = wo + (int64_t)(s0 + k) * D;
-      if constexpr (VPL % 4 == 0) {
-#pragma unroll
-        for (int i = 0; i < VPL; i += 4) {
-          const float4 v = *reinterpret_cast<const float4*>(src + i);
-          acc[i] = fmaf(wk, v.x, acc[i]);
-          acc[i + 1] = fmaf(wk, v.y, acc[i + 1]);
-          acc[i + 2] = fmaf(wk, v.z, acc[i + 2]);
-          acc[i + 3] = fmaf(wk, v.w, acc[i + 3]);
-        }
-      } else {
-#pragma unroll
-        for (int i = 0; i < VPL; i += 2) {
-          const float2 v = *reinterpret_cast<const float2*>(src + i);
-          acc[i] = fmaf(wk, v.x, acc[i]);
-          acc[i + 1] = fmaf(wk, v.y, acc[i + 1]);
-        }
-      }
-    }
-  }
-  T* op = reinterpret_cast<T*>(p.out) + (int64_t)it.qtok * p.o_st + (int64_t)qh * p.o_sh + lane * VPL;
-#pragma unroll
-  for (int i = 0; i < VPL; ++i) op[i] = Elem<T>::from_float(acc[i] / lsum);
-  if (lane == 0) p.lse[(int64_t)it.qtok * p.lse_st + qh] = mx * kLn2 + logf(lsum);
 }
 
 // ------------------------------------------------------------------ launching
@@ -665,6 +721,9 @@ constexpr int mma_stages() {
              : (227 * 1024 - 3 * 1024) / (kMmaWarps * TmaTile<D>::kStage);
 }
 constexpr int kSimtWarps = 4;
+
+// Bytes of the split counters at the end of the decode workspace.
+int64_t counter_bytes(int64_t num_items, int64_t hkv) { return ((num_items * hkv * 4 + 15) / 16) * 16; }
 
 int choose_bps(int num_items, int hkv, int64_t max_blocks, int requested) {
   if (requested > 0) return requested > kMaxBps ? kMaxBps : requested;
@@ -731,10 +790,7 @@ int launch_typed(const DecodeParams& p, int64_t n_warps, bool tensor_core, cudaS
   } else {
     rc = launch_simt_g<T, D>(p, n_warps, s);
   }
-  if (rc != SEB_OK || p.max_splits <= 1) return rc;
-  const int64_t combos = (int64_t)p.num_items * p.hq;
-  decode_combine_kernel<T, D><<<(unsigned)((combos + 3) / 4), 128, 0, s>>>(p);
-  return launch_status("decode_combine_kernel");
+  return rc;
 }
 
 template <typename T>
@@ -759,7 +815,8 @@ extern "C" int64_t seb_paged_decode_workspace_size(int32_t num_items, int32_t nu
   const int bps = choose_bps(num_items, num_kv_heads, max_blocks, blocks_per_split);
   const int64_t max_splits = (max_blocks + bps - 1) / bps;
   if (max_splits <= 1) return 0;
-  return (int64_t)num_items * num_q_heads * max_splits * (head_dim + 2) * (int64_t)sizeof(float);
+  return (int64_t)num_items * num_q_heads * max_splits * (head_dim + 2) * (int64_t)sizeof(float) +
+         seb::counter_bytes(num_items, num_kv_heads);
 }
 
 extern "C" int seb_paged_decode(const void* q, int64_t q_stride_token, int64_t q_stride_head,
@@ -831,6 +888,7 @@ extern "C" int seb_paged_decode(const void* q, int64_t q_stride_token, int64_t q
   p.err = err;
   p.ws_o = nullptr;
   p.ws_ml = nullptr;
+  p.counters = nullptr;
   if (p.max_splits > 1) {
     const int64_t need = seb_paged_decode_workspace_size(num_items, num_q_heads, num_kv_heads, head_dim,
                                                          max_blocks, blocks_per_split);
@@ -841,10 +899,14 @@ extern "C" int seb_paged_decode(const void* q, int64_t q_stride_token, int64_t q
     }
     p.ws_o = static_cast<float*>(workspace);
     p.ws_ml = p.ws_o + (int64_t)num_items * num_q_heads * p.max_splits * head_dim;
+    p.counters = reinterpret_cast<int32_t*>(static_cast<char*>(workspace) + need -
+                                            counter_bytes(num_items, num_kv_heads));
   }
   const int64_t n_warps = (int64_t)num_items * num_kv_heads * p.max_splits;
   SEB_CHECK_ARG((n_warps + 3) / 4 < (1ll << 31), "seb_paged_decode: grid too large");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (p.counters)
+    SEB_CHECK_CUDA(cudaMemsetAsync(p.counters, 0, (size_t)counter_bytes(num_items, num_kv_heads), s));
   switch (dtype) {
     case SEB_BF16: return launch_dim<__nv_bfloat16>(p, head_dim, n_warps, tc, s);
     case SEB_F16: return launch_dim<__half>(p, head_dim, n_warps, tc, s);

@@ -262,7 +262,7 @@ def paged_decode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, 
         lse.data_ptr(), lse.stride(0),
         ws.data_ptr(), ws.numel(), err_word(dev).data_ptr(), _stream(dev))
     check("seb_paged_decode", st)
-    LAUNCHES[0] += 2 if ws_bytes > 0 else 1  # split pass (+ combine pass when splits > 1)
+    LAUNCHES[0] += 1  # splits and their merge run in one launch
     _after(dev)
     return out, lse
 

@@ -99,7 +99,8 @@ def test_decode_workspace_size(lib):
     # one split per item -> no workspace
     assert lib.seb_paged_decode_workspace_size(64, 32, 8, 128, 8, 8) == 0
     n = lib.seb_paged_decode_workspace_size(64, 32, 8, 128, 512, 32)
-    assert n == 64 * 32 * 16 * (128 + 2) * 4
+    # partial O and (m, l) per split, then one int32 counter per (item, kv head)
+    assert n == 64 * 32 * 16 * (128 + 2) * 4 + 64 * 8 * 4
 
 
 def test_ctypes_signatures_match_header_arity():

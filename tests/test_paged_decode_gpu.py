@@ -129,11 +129,26 @@ def test_shapes_vs_oracle(dtype, hq, hkv, d):
 @pytest.mark.parametrize("bps", [1, 3, 8, 32])
 def test_split_sizes_agree(bps):
     """Every split size (1 block .. 32 blocks per split, hence 1 .. many splits and the
-    combine pass) gives the oracle's answer."""
+    in-kernel merge of the splits) gives the oracle's answer."""
     b = workloads.decode_batch(6, 1, 1200, 32, 8, 128, torch.bfloat16, seed=40 + bps, num_blocks=600)
     o, lse = run_b200(b, blocks_per_split=bps)
     o_ref, lse_ref = run_oracle(b)
     assert_close(o, lse, o_ref, lse_ref, torch.bfloat16)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_workspace_reuse_with_garbage(dtype):
+    """The split merge needs nothing in the shared workspace to start at zero: a
+    workspace full of junk, then calls of different shapes (so one call's split
+    counters land on another call's partial sums) all match the oracle."""
+    from serving_engine_b200 import ops
+    ops.workspace(torch.device(DEV), 64 << 20).fill_(0xA5)
+    shapes = [(40, 900, 32, 8), (3, 3000, 16, 2), (64, 700, 32, 8), (5, 2500, 8, 8)]
+    for i, (n, ctx, hq, hkv) in enumerate(shapes):
+        b = workloads.decode_batch(n, 1, ctx, hq, hkv, 128, dtype, seed=300 + i, num_blocks=n * (ctx // 16 + 2))
+        o, lse = run_b200(b, blocks_per_split=2 + i)
+        o_ref, lse_ref = run_oracle(b)
+        assert_close(o, lse, o_ref, lse_ref, dtype)
 
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
