@@ -6,27 +6,31 @@
 // runs 16x16 tiles per (q tile, row, q head) and reads the KV of a kv head once
 // per q head of its GQA group.
 //
-// One CTA computes a 128-row tile of one prefill row and one kv head; the 128
-// MMA rows pack (query, head) pairs of the GQA group, row m = query (m / G),
-// head (m % G), so each K/V tile is read once for the whole group:
-//   warp 0     TMA producer: the Q tile once, then K and V tiles of 128 keys
-//              (8 paged blocks, gathered through the block table) into 2-stage
-//              rings of 128B-swizzled K-major panels; K runs two tiles ahead of
-//              V, matching the order the MMAs consume them;
-//   warp 1     owns TMEM (512 columns: three S buffers at 0/128/256, O at 384)
-//              and issues the MMAs from one thread: S(j+2) = Q K(j+2)^T is
-//              issued before O += P(j) V(j), so two score tiles are always in
-//              flight while the softmax works on a third;
-//   warps 2-9  two softmax warpgroups; a thread owns half of one tile row
-//              (TMEM lane): read its 64 scores, mask boundary tiles, agree on
-//              the row max with its partner thread through shared memory,
-//              online softmax with a lazily rescaled reference max (O and l are
-//              only rescaled when a block max exceeds it by 2^8), write P as
-//              bf16 to a swizzled shared-memory tile, and finally normalise its
-//              half of O, store it and the LSE.
-// P V is split into a 16-bit high part and its 16-bit remainder for tiles
-// whose rows see fewer than kSplitBelow keys (early positions of a prompt),
-// where one rounding of P would cost more than the output tolerance.
+// One CTA computes two 128-row Q tiles of one prefill row and one kv head; the
+// 128 MMA rows of a Q tile pack (query, head) pairs of the GQA group, row
+// m = query (m / G), head (m % G), so each K/V tile is read once for the whole
+// group and feeds 256 rows. K/V tiles hold 64 keys (4 paged blocks).
+//   warp 0     TMA producer: the two Q tiles once, then K and V tiles gathered
+//              through the block table (block ids prefetched a window ahead)
+//              into 3-stage rings of 128B-swizzled panels; K runs three tiles
+//              ahead of V, matching the order the MMAs consume them;
+//   warp 1     owns TMEM (512 columns: two S buffers of 64 columns and one O
+//              accumulator per Q tile) and issues the MMAs from one thread:
+//              per KV tile j, O(t) += P(t, j) V(j) for both Q tiles, then
+//              S(t, j+2) = Q(t) K(j+2)^T, so the next scores are always ready;
+//   warps 2-9  one softmax warpgroup per Q tile; a thread owns one tile row
+//              (TMEM lane): read its 64 scores, mask boundary tiles, online
+//              softmax with a lazily rescaled reference max (O and l are only
+//              rescaled when a block max exceeds it by 2^8), write P as bf16 to
+//              a swizzled shared-memory tile (double-buffered, so P(j+1) is
+//              written while PV(j) runs), and finally normalise its row of O,
+//              store it and the LSE.
+// Two Q tiles per K/V tile halve the TMA traffic per FLOP: a paged K/V tile is
+// 16-row boxes (one per block and 128-byte panel), whose per-SM TMA rate, not
+// L2 bandwidth, bounds a one-Q-tile design.
+// P V is split into a 16-bit high part and its 16-bit remainder for CTAs
+// whose first row sees fewer than kSplitBelow keys (early positions of a
+// prompt), where one rounding of P would cost more than the output tolerance.
 //
 // Roofline: tensor. Algorithmic FLOPs per call = sum over rows, heads and
 // queries of 4 * head_dim * (visible keys of that query).
@@ -42,14 +46,17 @@ namespace {
 constexpr float kLn2p = 0.69314718055994530942f;
 constexpr float kLog2ep = 1.44269504088896340736f;
 constexpr unsigned kFullMask = 0xffffffffu;
-constexpr int kBM = 128;        // MMA rows per CTA
-constexpr int kBN = 128;        // keys per KV tile
-constexpr int kThreads = 320;   // producer, MMA, 8 softmax warps (2 warpgroups)
-constexpr int kRing = 2;        // K and V ring depths
-constexpr int kSBufs = 3;       // score buffers in TMEM
+constexpr int kBM = 128;       // MMA rows per Q tile
+constexpr int kBN = 128;       // keys per KV tile (8 paged blocks)
+constexpr int kQT = 2;         // Q tiles per CTA: each K/V tile feeds 256 rows
+constexpr int kThreads = 320;  // producer, MMA, one softmax warpgroup per Q tile
+constexpr int kKStages = 2;    // K ring depth
+constexpr int kVStages = 2;    // V ring depth
 constexpr int kTmemCols = 512;
-constexpr int kColS = 0;        // S buffers at columns 0, 128, 256
-constexpr int kColO = 384;      // O accumulator
+// TMEM columns of Q tile t: S at t * 128 (128 fp32 scores per row; P overwrites
+// its first 64 columns as packed 16-bit pairs), O at 256 + t * 128.
+constexpr int kColS = 0;
+constexpr int kColO = 256;
 constexpr float kLazyThreshold = 8.0f;
 constexpr int kSplitBelow = 256;
 
@@ -65,8 +72,8 @@ struct PrefillParams {
   int32_t num_rows;
   const int32_t* rows;
   int32_t num_prefill_rows;
-  int32_t mtiles;  // m-tiles per row (ceil(max_q_len / queries_per_tile))
-  int32_t hq, hkv, group, qpt;  // qpt = queries per tile = 128 / group
+  int32_t mpairs;  // Q-tile pairs per row: ceil(max_q_len / (2 * queries_per_tile))
+  int32_t hq, hkv, group, qpt;  // qpt = queries per Q tile = 128 / group
   float scale_log2;
   int32_t causal;
   char* out;
@@ -78,34 +85,29 @@ struct PrefillParams {
 
 template <int D>
 struct PrefillLayout {
-  static constexpr int kPanels = D / 64;
-  static constexpr int kPanel = 128 * 128;  // 128 rows x 128 bytes
+  static constexpr int kPanels = D / 64;      // 128-byte column panels of a row
+  static constexpr int kPanel = 128 * 128;    // 128 rows x 128 bytes
   static constexpr int kTileQ = kPanels * kPanel;
   static constexpr int kTileKV = kPanels * kPanel;
-  static constexpr int kTileP = 2 * kPanel;  // 128 rows x 128 keys
-  static constexpr int oQ = 0;
-  static constexpr int oK = oQ + kTileQ;
-  static constexpr int oV = oK + kRing * kTileKV;
-  static constexpr int oP = oV + kRing * kTileKV;
-  static constexpr int oPlo = oP + kTileP;  // P's 16-bit remainder (split tiles)
-  static constexpr int oBar = oPlo + kTileP;
-  static constexpr int oX = oBar + 256;  // row max / sum exchange between the two softmax warpgroups
-  static constexpr int kBytes = oX + 2 * 128 * 4;
+  static constexpr int oQ = 0;                // [Q tile]
+  static constexpr int oK = oQ + kQT * kTileQ;  // [stage]
+  static constexpr int oV = oK + kKStages * kTileKV;
+  static constexpr int oBar = oV + kVStages * kTileKV;
+  static constexpr int kBytes = oBar + 256;
 };
 
 // mbarrier slots
 enum {
   kBarQ = 0,
-  kBarKFull = 1,    // +stage
-  kBarVFull = 3,    // +stage
-  kBarKEmpty = 5,   // +stage: S of the tile has consumed K
-  kBarVEmpty = 7,   // +stage: PV of the tile has consumed V
-  kBarSFull = 9,    // +S buffer (3)
-  kBarSFree = 12,   // +S buffer (3)
-  kBarPFull = 15,
-  kBarPFree = 16,   // one completion per PV (P buffer free, O stable)
-  kBarDone = 17,
-  kNumBars = 18
+  kBarKFull = 1,   // +stage (2)
+  kBarKEmpty = 3,  // +stage: S of every Q tile consumed K
+  kBarVFull = 5,   // +stage (2)
+  kBarVEmpty = 7,  // +stage: PV of every Q tile consumed V
+  kBarSFull = 9,   // +Q tile: S(t, j) complete (and every earlier MMA)
+  kBarPFull = 11,  // +Q tile: the tile's 4 softmax warps stored P(t, j)
+  kBarPFree = 13,  // +Q tile: PV(t, j) complete: S/P columns reusable, O final
+  kBarDone = 15,
+  kNumBars = 16
 };
 
 // 2^x by the MUFU instruction (ex2.approx.ftz: 2^-22 relative error, -inf -> +0).
@@ -115,10 +117,6 @@ __device__ __forceinline__ float fast_exp2(float x) {
   return y;
 }
 
-__device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
-  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
-}
-
 __device__ __forceinline__ bool wait_or_flag(uint32_t bar, uint32_t parity, bool& failed) {
   if (failed) return false;
   if (!mbar_wait_bounded(bar, parity)) {
@@ -126,6 +124,20 @@ __device__ __forceinline__ bool wait_or_flag(uint32_t bar, uint32_t parity, bool
     return false;
   }
   return true;
+}
+
+// Scores of keys [key0, key0 + 32) of one row, masked in place when the tile is
+// not fully visible: keys past the row's visible range -> -inf, the reference's
+// zero-padded keys of the last block (past k_len) -> 0; scaled by c when masked.
+__device__ __forceinline__ void mask_chunk(float (&x)[32], int key0, int vis, int k_len, float c) {
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    const int key = key0 + i;
+    float v = x[i] * c;
+    if (key >= vis) v = -INFINITY;
+    else if (key >= k_len) v = 0.f;
+    x[i] = v;
+  }
 }
 
 template <typename T, int D>
@@ -141,26 +153,38 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
 
-  // ---- tile coordinates (m-tiles of a row visited late-first: they are the longest)
+  // ---- work unit: (prefill row, kv head, pair of Q tiles, half). Pairs are
+  // visited late-first (they are the longest). Half 0 runs both Q tiles of the
+  // pair; a pair whose first query sees fewer than kSplitBelow keys needs P's
+  // remainder and runs one Q tile per CTA instead: half 0 the first, half 1 the
+  // second. Half-1 CTAs of other pairs exit at once.
   int bx = blockIdx.x;
-  const int mt = p.mtiles - 1 - (bx % p.mtiles);
-  bx /= p.mtiles;
+  const int half = bx & 1;
+  bx >>= 1;
+  const int pr = p.mpairs - 1 - (bx % p.mpairs);
+  bx /= p.mpairs;
   const int kvh = bx % p.hkv;
   const int prow = bx / p.hkv;
   if (prow >= p.num_prefill_rows) return;
   const int row = p.rows ? __ldg(p.rows + prow) : prow;
   if (row < 0 || row >= p.num_rows) {
-    if (threadIdx.x == 0 && kvh == 0 && mt == 0) atomic_or_err(p.err, SEB_ERRBIT_META);
+    if (threadIdx.x == 0 && kvh == 0 && pr == 0 && half == 0) atomic_or_err(p.err, SEB_ERRBIT_META);
     return;
   }
   const int q_len = __ldg(p.q_lens + row);
   const int q_start = __ldg(p.q_starts + row);
   const int k_len = max(__ldg(p.k_lens + row), 0);
   const int qpos0 = __ldg(p.q_pos + row);
-  const int i0 = mt * p.qpt;
-  if (i0 >= q_len) return;
-  const int i_last = min(i0 + p.qpt, q_len) - 1;
   const int ceil16 = (k_len + 15) & ~15;
+  const int pair0 = pr * kQT * p.qpt;  // first query of the pair
+  if (pair0 >= q_len) return;
+  const bool has_second = pair0 + p.qpt < q_len;
+  const bool pair_split = (p.causal ? min(ceil16, qpos0 + pair0 + 1) : ceil16) < kSplitBelow;
+  if (half == 1 && !(pair_split && has_second)) return;
+  const int i0 = pair0 + half * p.qpt;                      // first query of this CTA
+  const int nqt = (half == 0 && has_second && !pair_split) ? 2 : 1;  // Q tiles of this CTA
+  const bool split = (p.causal ? min(ceil16, qpos0 + i0 + 1) : ceil16) < kSplitBelow;
+  const int i_last = min(i0 + nqt * p.qpt, q_len) - 1;
   int nvis_tile = p.causal ? min(ceil16, qpos0 + i_last + 1) : ceil16;
   nvis_tile = max(nvis_tile, 0);
   int nblk = (nvis_tile + 15) >> 4;
@@ -170,20 +194,20 @@ __global__ void __launch_bounds__(kThreads, 1)
     nvis_tile = nblk * 16;
   }
   const int ntiles = (nblk + 7) >> 3;
-  const int min_vis = p.causal ? min(ceil16, qpos0 + i0 + 1) : ceil16;
-  const bool split = min_vis < kSplitBelow;
   const int G = p.group;
 
-  // Softmax-thread row identity (also used by the no-key epilogue).
+  // Softmax-thread identity: warpgroup `qt` owns Q tile qt; a thread owns one
+  // MMA row (TMEM lane) m = query (m / G), head (m % G).
+  const int qt = (warp - 2) >> 2;
   const int q4 = warp & 3;
   const int m = q4 * 32 + lane;
-  const int qi = i0 + m / G;
+  const int qi = i0 + qt * p.qpt + m / G;
   const int gh = m % G;
-  const bool row_valid = (warp >= 2) && qi <= i_last;
+  const bool row_valid = (warp >= 2) && qt < nqt && qi <= i_last;
 
   if (ntiles == 0) {
     // No visible keys: the reference's loop never runs, O = 0/0, LSE = -inf.
-    if (row_valid && warp < 6) {
+    if (row_valid) {
       T* op = reinterpret_cast<T*>(p.out) + (int64_t)(q_start + qi) * p.o_st + (int64_t)(kvh * G + gh) * p.o_sh;
       for (int d = 0; d < D; ++d) op[d] = Elem<T>::from_float(__int_as_float(0x7fc00000));
       p.lse[(int64_t)(q_start + qi) * p.lse_st + kvh * G + gh] = -INFINITY;
@@ -195,18 +219,19 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sbase + L::oBar + 8 * kNumBars);
   if (threadIdx.x == 0) {
     mbar_init(bar + 8 * kBarQ, 1);
-    for (int s = 0; s < kRing; ++s) {
+    for (int s = 0; s < kKStages; ++s) {
       mbar_init(bar + 8 * (kBarKFull + s), 1);
-      mbar_init(bar + 8 * (kBarVFull + s), 1);
       mbar_init(bar + 8 * (kBarKEmpty + s), 1);
+    }
+    for (int s = 0; s < kVStages; ++s) {
+      mbar_init(bar + 8 * (kBarVFull + s), 1);
       mbar_init(bar + 8 * (kBarVEmpty + s), 1);
     }
-    for (int b = 0; b < kSBufs; ++b) {
-      mbar_init(bar + 8 * (kBarSFull + b), 1);
-      mbar_init(bar + 8 * (kBarSFree + b), 8);
+    for (int t = 0; t < kQT; ++t) {
+      mbar_init(bar + 8 * (kBarSFull + t), 1);
+      mbar_init(bar + 8 * (kBarPFull + t), 4);
+      mbar_init(bar + 8 * (kBarPFree + t), 1);
     }
-    mbar_init(bar + 8 * kBarPFull, 8);
-    mbar_init(bar + 8 * kBarPFree, 1);
     mbar_init(bar + 8 * kBarDone, 1);
     fence_mbar_init();
   }
@@ -226,26 +251,43 @@ __global__ void __launch_bounds__(kThreads, 1)
       prefetch_tensor_map(&tmap_q);
       prefetch_tensor_map(&tmap_k);
       prefetch_tensor_map(&tmap_v);
-      mbar_arrive_expect_tx(bar + 8 * kBarQ, L::kTileQ);
+      mbar_arrive_expect_tx(bar + 8 * kBarQ, nqt * L::kTileQ);
+      for (int t = 0; t < nqt; ++t)
 #pragma unroll
-      for (int pn = 0; pn < L::kPanels; ++pn)
-        tma_load_3d(base + L::oQ + pn * L::kPanel, &tmap_q, pn * 64, kvh * G, q_start + i0, bar + 8 * kBarQ);
+        for (int pn = 0; pn < L::kPanels; ++pn)
+          tma_load_3d(base + L::oQ + t * L::kTileQ + pn * L::kPanel, &tmap_q, pn * 64, kvh * G,
+                      q_start + i0 + t * p.qpt, bar + 8 * kBarQ);
     }
     const int32_t* bt = p.block_table + (int64_t)row * p.bt_stride;
-    // Load K (is_v = 0) or V (is_v = 1) of tile j into stage j % 2.
+    // Block ids are read a window of 4 tiles (32 blocks, one per lane) ahead of
+    // their use, so the copies never wait on a block-table load. K and V keep
+    // their own windows.
+    auto fetch = [&](int w) -> int {
+      const int blk = 32 * w + lane;
+      return blk < nblk ? __ldg(bt + blk) : 0;
+    };
+    int kcur = fetch(0), knext = fetch(1), kw = 0;
+    int vcur = kcur, vnext = knext, vw = 0;
+    auto block_id = [&](int t, int& cur, int& next, int& w) -> int {
+      while (w < (t >> 2)) {
+        cur = next;
+        next = fetch(w + 2);
+        ++w;
+      }
+      return __shfl_sync(kFullMask, cur, ((t & 3) << 3) + (lane & 7));
+    };
+    // Load K (is_v = 0) or V (is_v = 1) of tile j (8 blocks) into its ring stage.
     auto load = [&](int j, int is_v) -> bool {
-      const int s = j & 1;
-      const int u = j >> 1;
+      const int stages = is_v ? kVStages : kKStages;
+      const int s = j % stages;
+      const int u = j / stages;
+      int bid = is_v ? block_id(j, vcur, vnext, vw) : block_id(j, kcur, knext, kw);
       if (u >= 1 && !wait_or_flag(bar + 8 * ((is_v ? kBarVEmpty : kBarKEmpty) + s), (u - 1) & 1, failed))
         return false;
       const int nb = min(8, nblk - 8 * j);
-      int bid = 0;
-      if (lane < nb) {
-        bid = __ldg(bt + 8 * j + lane);
-        if (bid < 0 || (int64_t)bid >= p.num_blocks) {
-          atomic_or_err(p.err, SEB_ERRBIT_BLOCK_ID);
-          bid = 0;  // read a real block instead; the row's result is flagged as invalid
-        }
+      if (lane < nb && (bid < 0 || (int64_t)bid >= p.num_blocks)) {
+        atomic_or_err(p.err, SEB_ERRBIT_BLOCK_ID);
+        bid = 0;  // read a real block instead; the row's result is flagged as invalid
       }
       const uint32_t fb = bar + 8 * ((is_v ? kBarVFull : kBarKFull) + s);
       if (lane == 0) mbar_arrive_expect_tx(fb, nb * L::kPanels * 2048);
@@ -258,57 +300,76 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       return true;
     };
-    // Consumption order of the MMA warp: K(0), K(1), then per tile j K(j+2), V(j).
+    // The MMA warp consumes K(0), then per tile j V(j) and K(j+1).
     int k_issued = 0, v_issued = 0;
-    for (int j = 0; j < min(2, ntiles); ++j)
-      if (load(j, 0)) ++k_issued;
     for (int j = 0; j < ntiles && !failed; ++j) {
+      if (load(j, 0)) ++k_issued;
       if (load(j, 1)) ++v_issued;
-      if (j + 2 < ntiles && load(j + 2, 0)) ++k_issued;
     }
     // Leave no copy in flight: the last loads must have landed.
-    for (int j = max(0, k_issued - kRing); j < k_issued; ++j)
-      mbar_wait_bounded(bar + 8 * (kBarKFull + (j & 1)), (j >> 1) & 1, 1u << 16);
-    for (int j = max(0, v_issued - kRing); j < v_issued; ++j)
-      mbar_wait_bounded(bar + 8 * (kBarVFull + (j & 1)), (j >> 1) & 1, 1u << 16);
+    for (int j = max(0, k_issued - kKStages); j < k_issued; ++j)
+      mbar_wait_bounded(bar + 8 * (kBarKFull + j % kKStages), (j / kKStages) & 1, 1u << 16);
+    for (int j = max(0, v_issued - kVStages); j < v_issued; ++j)
+      mbar_wait_bounded(bar + 8 * (kBarVFull + j % kVStages), (j / kVStages) & 1, 1u << 16);
   } else if (warp == 1) {
     // ---------------------------------------------------------------- MMA
     constexpr uint32_t idesc_qk = tc::idesc_f16(kBf16, false, kBM, kBN);
     constexpr uint32_t idesc_pv = tc::idesc_f16(kBf16, true, kBM, D);
     wait_or_flag(bar + 8 * kBarQ, 0, failed);
-    auto issue_s = [&](int j) {
-      const int s = j & 1;
-      const int b = j % kSBufs;
-      const int u = j / kSBufs;
-      if (!wait_or_flag(bar + 8 * (kBarKFull + s), (j >> 1) & 1, failed)) return;
-      if (u >= 1 && !wait_or_flag(bar + 8 * (kBarSFree + b), (u - 1) & 1, failed)) return;
-      tc::fence_after_sync();
+    // S(t, j) = Q(t) K(j)^T into the S/P columns of Q tile t.
+    auto issue_s = [&](int t, int j) {
+      const int s = j % kKStages;
       if (lane == 0) {
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
-          const uint64_t a = tc::smem_desc_sw128(base + L::oQ + (kk >> 2) * L::kPanel + (kk & 3) * 32, 16, 1024);
-          const uint64_t bd =
-              tc::smem_desc_sw128(base + L::oK + s * L::kTileKV + (kk >> 2) * L::kPanel + (kk & 3) * 32, 16, 1024);
-          tc::mma_ss(tmem + kColS + b * kBN, a, bd, idesc_qk, kk > 0);
+          const uint64_t a = tc::smem_desc_sw128(
+              base + L::oQ + t * L::kTileQ + (kk >> 2) * L::kPanel + (kk & 3) * 32, 16, 1024);
+          const uint64_t bd = tc::smem_desc_sw128(
+              base + L::oK + s * L::kTileKV + (kk >> 2) * L::kPanel + (kk & 3) * 32, 16, 1024);
+          tc::mma_ss(tmem + kColS + t * 128, a, bd, idesc_qk, kk > 0);
         }
-        tc::commit(bar + 8 * (kBarSFull + b));
-        tc::commit(bar + 8 * (kBarKEmpty + s));
+        tc::commit(bar + 8 * (kBarSFull + t));
       }
       __syncwarp();
     };
-    for (int j = 0; j < min(2, ntiles) && !failed; ++j) issue_s(j);
+    // O(t) += P(t, j) V(j), P read from TMEM.
+    auto issue_pv = [&](int t, int j) {
+      const int s = j % kVStages;
+      if (lane == 0) {
+#pragma unroll
+        for (int kk = 0; kk < kBN / 16; ++kk) {
+          const uint64_t bd = tc::smem_desc_sw128(base + L::oV + s * L::kTileKV + kk * 2048, L::kPanel, 1024);
+          tc::mma_ts(tmem + kColO + t * 128, tmem + kColS + t * 128 + 8 * kk, bd, idesc_pv, j > 0 || kk > 0);
+        }
+        if (split) {  // P's remainder, in the (idle) second Q tile's S columns
+#pragma unroll
+          for (int kk = 0; kk < kBN / 16; ++kk) {
+            const uint64_t bd = tc::smem_desc_sw128(base + L::oV + s * L::kTileKV + kk * 2048, L::kPanel, 1024);
+            tc::mma_ts(tmem + kColO + t * 128, tmem + kColS + 128 + 8 * kk, bd, idesc_pv, true);
+          }
+        }
+        tc::commit(bar + 8 * (kBarPFree + t));
+      }
+      __syncwarp();
+    };
+    // Ping-pong: per KV tile j and Q tile t, PV(t, j) then S(t, j+1), so one Q
+    // tile's softmax runs while the other tile's MMAs execute. S(t, j+1)
+    // overwrites the columns PV(t, j) reads P from: it waits for PV(t, j).
+    if (wait_or_flag(bar + 8 * kBarKFull, 0, failed)) {
+      for (int t = 0; t < nqt; ++t) issue_s(t, 0);
+      if (lane == 0) tc::commit(bar + 8 * kBarKEmpty);
+      __syncwarp();
+    }
     for (int j = 0; j < ntiles && !failed; ++j) {
-      if (j + 2 < ntiles) issue_s(j + 2);
-      if (failed) break;
-      const int s = j & 1;
-      if (!wait_or_flag(bar + 8 * (kBarVFull + s), (j >> 1) & 1, failed)) break;
+      const int sv = j % kVStages;
+      if (!wait_or_flag(bar + 8 * (kBarVFull + sv), (j / kVStages) & 1, failed)) break;
       // Rows of this tile that hold real keys: loaded (nblk) and below k_len.
       const int r0 = min(max(k_len - j * kBN, 0), min(8, nblk - 8 * j) * 16);
       if (r0 < kBN) {
         // V rows of padding keys must be exact zeros (their P is 0 or, for the
         // reference's zero-padded keys, exp(-m)); the pool past k_len and the
         // rows of blocks this tile did not load may hold anything.
-        char* vt = sbase + L::oV + s * L::kTileKV;
+        char* vt = sbase + L::oV + sv * L::kTileKV;
         for (int c = lane; c < (kBN - r0) * L::kPanels * 8; c += 32) {
           const int r = r0 + c / (L::kPanels * 8);
           const int rem = c % (L::kPanels * 8);
@@ -317,25 +378,21 @@ __global__ void __launch_bounds__(kThreads, 1)
         fence_proxy_async_smem();
         __syncwarp();
       }
-      if (!wait_or_flag(bar + 8 * kBarPFull, j & 1, failed)) break;
-      tc::fence_after_sync();
+      const bool next = j + 1 < ntiles;
+      const int sk = (j + 1) % kKStages;
+      for (int t = 0; t < nqt && !failed; ++t) {
+        if (!wait_or_flag(bar + 8 * (kBarPFull + t), j & 1, failed)) break;
+        tc::fence_after_sync();
+        issue_pv(t, j);
+        if (!next) continue;
+        if (t == 0 && !wait_or_flag(bar + 8 * (kBarKFull + sk), ((j + 1) / kKStages) & 1, failed)) break;
+        if (!wait_or_flag(bar + 8 * (kBarPFree + t), j & 1, failed)) break;
+        tc::fence_after_sync();
+        issue_s(t, j + 1);
+      }
       if (lane == 0) {
-#pragma unroll
-        for (int kk = 0; kk < kBN / 16; ++kk) {
-          const uint64_t a = tc::smem_desc_sw128(base + L::oP + (kk >> 2) * L::kPanel + (kk & 3) * 32, 16, 1024);
-          const uint64_t bd = tc::smem_desc_sw128(base + L::oV + s * L::kTileKV + kk * 2048, L::kPanel, 1024);
-          tc::mma_ss(tmem + kColO, a, bd, idesc_pv, j > 0 || kk > 0);
-        }
-        if (split) {
-#pragma unroll
-          for (int kk = 0; kk < kBN / 16; ++kk) {
-            const uint64_t a = tc::smem_desc_sw128(base + L::oPlo + (kk >> 2) * L::kPanel + (kk & 3) * 32, 16, 1024);
-            const uint64_t bd = tc::smem_desc_sw128(base + L::oV + s * L::kTileKV + kk * 2048, L::kPanel, 1024);
-            tc::mma_ss(tmem + kColO, a, bd, idesc_pv, true);
-          }
-        }
-        tc::commit(bar + 8 * kBarPFree);
-        tc::commit(bar + 8 * (kBarVEmpty + s));
+        tc::commit(bar + 8 * (kBarVEmpty + sv));
+        if (next) tc::commit(bar + 8 * (kBarKEmpty + sk));
       }
       __syncwarp();
     }
@@ -343,74 +400,46 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) tc::commit(bar + 8 * kBarDone);
     __syncwarp();
     mbar_wait_bounded(bar + 8 * kBarDone, 0, 1u << 20);
-  } else {
+  } else if (qt < nqt) {
     // ------------------------------------------------------------ softmax
-    // Two warpgroups share each tile row: `half` 0 owns keys / O columns 0..D/2-1
-    // of its row, half 1 the rest. Warps w and w+4 see the same TMEM lanes (w % 4).
-    const int half = (warp - 2) >> 2;
     const uint32_t taddr = tmem + ((uint32_t)(q4 * 32) << 16);
+    const uint32_t col_s = kColS + qt * 128;
+    const uint32_t col_o = kColO + qt * 128;
     const int pos = qpos0 + qi;
     const int vis = row_valid ? (p.causal ? min(ceil16, pos + 1) : ceil16) : 0;
+    const int min_vis = p.causal ? min(ceil16, qpos0 + i0 + qt * p.qpt + 1) : ceil16;
     const float c = p.scale_log2;
-    float* xchg = reinterpret_cast<float*>(sbase + L::oX);  // [half][128]: row maxima per tile, then sums
     float m_ref = -INFINITY;
     float l = 0.f;
-    char* ph = sbase + L::oP + half * L::kPanel + m * 128;
-    char* pl = sbase + L::oPlo + half * L::kPanel + m * 128;
     // After a failed (timed-out) wait the loop keeps its shape with the waits
-    // skipped, so both warpgroups still meet at every named barrier.
+    // skipped; warp-collective TMEM accesses stay warp-uniform.
     for (int j = 0; j < ntiles; ++j) {
-      const int b = j % kSBufs;
-      wait_or_flag(bar + 8 * (kBarSFull + b), (j / kSBufs) & 1, failed);
+      // S(t, j) complete; its commit also covers PV(t, j-1), so O is stable.
+      wait_or_flag(bar + 8 * (kBarSFull + qt), j & 1, failed);
       tc::fence_after_sync();
-      float x[64];
-      {
-        float v[32];
-        tc::tmem_ld32(taddr + kColS + b * kBN + half * 64, v);
-#pragma unroll
-        for (int i = 0; i < 32; ++i) x[i] = v[i];
-        tc::tmem_ld32(taddr + kColS + b * kBN + half * 64 + 32, v);
-#pragma unroll
-        for (int i = 0; i < 32; ++i) x[32 + i] = v[i];
-      }
-      tc::tmem_wait_ld();
-      tc::fence_before_sync();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(bar + 8 * (kBarSFree + b));
-
-      // Tiles every valid row sees in full need no mask: scores stay raw and
-      // the scale folds into the exponent's FMA. Boundary tiles are masked and
-      // scaled here (keys past the row's visible range: -inf; zero-padded keys
-      // of the last block: 0).
+      // Tiles every valid row of the Q tile sees in full need no mask: scores
+      // stay raw and the scale folds into the exponent's FMA.
       const bool full = (j + 1) * kBN <= min_vis && (j + 1) * kBN <= k_len;
-      float cm = c;
-      if (!full) {
-        const int kbase = j * kBN + half * 64;
+      const float cm = full ? c : 1.f;
+      // The row's 128 scores in one TMEM round trip.
+      float x[4][32];
 #pragma unroll
-        for (int i = 0; i < 64; ++i) {
-          const int key = kbase + i;
-          float v = x[i] * c;
-          if (key >= vis) v = -INFINITY;
-          else if (key >= k_len) v = 0.f;
-          x[i] = v;
-        }
-        cm = 1.f;
+      for (int ch = 0; ch < 4; ++ch) tc::tmem_ld32(taddr + col_s + 32 * ch, x[ch]);
+      tc::tmem_wait_ld();
+      if (!full) {
+#pragma unroll
+        for (int ch = 0; ch < 4; ++ch) mask_chunk(x[ch], j * kBN + 32 * ch, vis, k_len, c);
       }
       float mx[8];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) mx[i] = fmaxf(x[i], x[8 + i]);
+      for (int i = 0; i < 8; ++i) mx[i] = fmaxf(fmaxf(x[0][i], x[0][8 + i]), fmaxf(x[0][16 + i], x[0][24 + i]));
 #pragma unroll
-      for (int i = 16; i < 64; i += 8)
+      for (int ch = 1; ch < 4; ++ch)
 #pragma unroll
-        for (int k = 0; k < 8; ++k) mx[k] = fmaxf(mx[k], x[i + k]);
-      float mloc = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])), fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
-      mloc *= cm;
-      // Row max over both halves (second barrier: both reads done before the
-      // next tile's writes).
-      xchg[half * 128 + m] = mloc;
-      named_bar_sync(1 + q4, 64);
-      const float mb = fmaxf(mloc, xchg[(1 - half) * 128 + m]);
-      named_bar_sync(1 + q4, 64);
+        for (int i = 0; i < 8; ++i)
+          mx[i] = fmaxf(mx[i], fmaxf(fmaxf(x[ch][i], x[ch][8 + i]), fmaxf(x[ch][16 + i], x[ch][24 + i])));
+      const float mb =
+          cm * fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])), fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
       const bool need = mb > m_ref + kLazyThreshold;
       float factor = 1.f;
       if (need) {
@@ -418,63 +447,67 @@ __global__ void __launch_bounds__(kThreads, 1)
         l *= factor;
         m_ref = mb;
       }
-      // PV(j-1) must be complete: it reads the P buffers and accumulates O.
-      if (j > 0) wait_or_flag(bar + 8 * kBarPFree, (j - 1) & 1, failed);
-      tc::fence_after_sync();
-      if (j > 0 && __any_sync(kFullMask, need)) {
-        // warp-collective: rows that keep their reference max scale by 1
-#pragma unroll
-        for (int cc = 0; cc < D / 64; ++cc) {
-          float o[32];
-          const uint32_t a = taddr + kColO + half * (D / 2) + 32 * cc;
-          tc::tmem_ld32(a, o);
-          tc::tmem_wait_ld();
-#pragma unroll
-          for (int i = 0; i < 32; ++i) o[i] *= factor;
-          tc::tmem_st32(a, o);
-        }
-        tc::tmem_wait_st();
-      }
+      // P = 2^(s - m) as 16-bit pairs over the first 64 S columns (already read),
+      // its remainder (split CTAs) in the second Q tile's columns.
       const float neg_m = m_ref == -INFINITY ? 0.f : -m_ref;
       float ls[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-      for (int ch = 0; ch < 8; ++ch) {
-        uint32_t hi[4], lo[4];
+      for (int ch = 0; ch < 4; ++ch) {
+        {
+          uint32_t hi[16];
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float a0 = fast_exp2(fmaf(x[8 * ch + 2 * e], cm, neg_m));
-          const float a1 = fast_exp2(fmaf(x[8 * ch + 2 * e + 1], cm, neg_m));
-          ls[e] += a0 + a1;
-          hi[e] = Mma<T>::pack(a0, a1);
-          if (split) {
-            const float2 f = Mma<T>::unpack(hi[e]);
-            lo[e] = Mma<T>::pack(a0 - f.x, a1 - f.y);
+          for (int e = 0; e < 16; ++e) {
+            const float a0 = fast_exp2(fmaf(x[ch][2 * e], cm, neg_m));
+            const float a1 = fast_exp2(fmaf(x[ch][2 * e + 1], cm, neg_m));
+            ls[e & 3] += a0 + a1;
+            hi[e] = Mma<T>::pack(a0, a1);
+            x[ch][2 * e] = a0;  // probabilities replace the consumed scores
+            x[ch][2 * e + 1] = a1;
           }
+          tc::tmem_st16u(taddr + col_s + 16 * ch, hi);
         }
-        const int off = ((ch ^ (m & 7))) << 4;
-        *reinterpret_cast<uint4*>(ph + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-        if (split) *reinterpret_cast<uint4*>(pl + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+        if (split) {  // remainder p - round16(p), recomputed from the probabilities
+          uint32_t lo[16];
+#pragma unroll
+          for (int e = 0; e < 16; ++e) {
+            const float2 f = Mma<T>::unpack(Mma<T>::pack(x[ch][2 * e], x[ch][2 * e + 1]));
+            lo[e] = Mma<T>::pack(x[ch][2 * e] - f.x, x[ch][2 * e + 1] - f.y);
+          }
+          tc::tmem_st16u(taddr + kColS + 128 + 16 * ch, lo);
+        }
       }
       l += (ls[0] + ls[1]) + (ls[2] + ls[3]);
-      fence_proxy_async_smem();
+      // O is stable (the S commit covers PV(t, j-1)); PV(t, j) is issued only
+      // after this thread's P arrival, so the rescale may come last.
+      if (j > 0 && __any_sync(kFullMask, need)) {
+        // warp-collective: rows that keep their reference max scale by 1
+#pragma unroll 1
+        for (int cc = 0; cc < D / 16; ++cc) {
+          float o[16];
+          const uint32_t a = taddr + col_o + 16 * cc;
+          tc::tmem_ld16(a, o);
+          tc::tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 16; ++i) o[i] *= factor;
+          tc::tmem_st16(a, o);
+        }
+      }
+      tc::tmem_wait_st();
       tc::fence_before_sync();
       __syncwarp();
-      if (lane == 0) mbar_arrive(bar + 8 * kBarPFull);
+      if (lane == 0) mbar_arrive(bar + 8 * (kBarPFull + qt));
     }
     // ------------------------------------------------------------ epilogue
-    wait_or_flag(bar + 8 * kBarPFree, (ntiles - 1) & 1, failed);
+    // Every MMA, the last PV of this Q tile included, has completed.
+    wait_or_flag(bar + 8 * kBarDone, 0, failed);
     tc::fence_after_sync();
-    xchg[half * 128 + m] = l;
-    named_bar_sync(1 + q4, 64);
     if (!__any_sync(kFullMask, failed)) {  // warp-uniform: tcgen05.ld is warp-collective
-      const float l_tot = l + xchg[(1 - half) * 128 + m];
-      const float inv = 1.f / l_tot;
-      T* op = reinterpret_cast<T*>(p.out) + (int64_t)(q_start + qi) * p.o_st + (int64_t)(kvh * G + gh) * p.o_sh +
-              half * (D / 2);
+      const float inv = 1.f / l;
+      T* op = reinterpret_cast<T*>(p.out) + (int64_t)(q_start + qi) * p.o_st + (int64_t)(kvh * G + gh) * p.o_sh;
 #pragma unroll
-      for (int cc = 0; cc < D / 64; ++cc) {
+      for (int cc = 0; cc < D / 32; ++cc) {
         float o[32];
-        tc::tmem_ld32(taddr + kColO + half * (D / 2) + 32 * cc, o);
+        tc::tmem_ld32(taddr + col_o + 32 * cc, o);
         tc::tmem_wait_ld();
         if (row_valid) {
 #pragma unroll
@@ -486,8 +519,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
-      if (row_valid && half == 0)
-        p.lse[(int64_t)(q_start + qi) * p.lse_st + kvh * G + gh] = m_ref * kLn2p + logf(l_tot);
+      if (row_valid) p.lse[(int64_t)(q_start + qi) * p.lse_st + kvh * G + gh] = m_ref * kLn2p + logf(l);
     }
   }
 
@@ -524,7 +556,7 @@ int launch_prefill(const PrefillParams& p, const void* q, int64_t q_st, int64_t 
   if (rc != SEB_OK) return rc;
   rc = kv_tensor_map(&tv, vc, dtype, p.num_blocks, p.hkv, D);
   if (rc != SEB_OK) return rc;
-  const int64_t grid = (int64_t)p.num_prefill_rows * p.hkv * p.mtiles;
+  const int64_t grid = (int64_t)p.num_prefill_rows * p.hkv * p.mpairs * 2;
   kern<<<(unsigned)grid, kThreads, smem, s>>>(p, tq, tk, tv);
   return launch_status("prefill_tc_kernel");
 }
@@ -586,7 +618,7 @@ extern "C" int seb_paged_prefill(const void* q, int64_t q_stride_token, int64_t 
   p.hkv = num_kv_heads;
   p.group = group;
   p.qpt = 128 / group;
-  p.mtiles = (max_q_len + p.qpt - 1) / p.qpt;
+  p.mpairs = (max_q_len + kQT * p.qpt - 1) / (kQT * p.qpt);
   p.scale_log2 = scale * kLog2ep;
   p.causal = is_causal ? 1 : 0;
   p.out = static_cast<char*>(out);
@@ -595,7 +627,7 @@ extern "C" int seb_paged_prefill(const void* q, int64_t q_stride_token, int64_t 
   p.lse = lse;
   p.lse_st = lse_stride_token;
   p.err = err;
-  const int64_t grid = (int64_t)num_prefill_rows * num_kv_heads * p.mtiles;
+  const int64_t grid = (int64_t)num_prefill_rows * num_kv_heads * p.mpairs * 2;
   SEB_CHECK_ARG(grid < (1ll << 31), "seb_paged_prefill: grid too large");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (dtype == SEB_BF16) {
