@@ -197,6 +197,42 @@ SEB_API int seb_paged_decode_noalloc(const void* q, int64_t q_stride_token, int6
                                      void* out, int64_t out_stride_token, int64_t out_stride_head,
                                      float* lse, int64_t lse_stride_token, int32_t* err, void* stream);
 
+/* ------------------------------------------------------------------------
+ * Decode-layer fusions used by the tensor-parallel decode driver (config 5).
+ * The reference runs one GPU and leaves these steps to the HF model's eager
+ * ops; the first folds HF's rotary embedding (apply_rotary_pos_emb, the
+ * rotate-half form) into _PagedKVCache.write (serving_engine/model_runner.py:21-32).
+ * All take bf16 or fp16 tensors with unit stride inside a row.
+ * ------------------------------------------------------------------------ */
+
+/* qkv: [n_tokens] rows of (num_q_heads + 2 * num_kv_heads) * head_dim elements:
+ * q heads, then k heads, then v heads. cos/sin: [n_tokens, head_dim]. Writes
+ * q rotated to q_out [n_tokens, num_q_heads, head_dim] (token stride given, heads
+ * contiguous) and the rotated k and the v of token t to pool slot
+ * slot_mapping[t] of k_cache / v_cache ([num_blocks * 16, num_kv_heads,
+ * head_dim]). out = x * cos + rotate_half(x) * sin with each product and the
+ * sum rounded to the element type, bit-identical to the eager tensor ops.
+ * Out-of-range slots set SEB_ERRBIT_SLOT and skip that token's K/V rows. */
+SEB_API int seb_rope_kv_append(const void* qkv, int64_t qkv_stride_token, int64_t n_tokens,
+                               int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
+                               const void* cos, const void* sin, int64_t cos_sin_stride_token,
+                               const int64_t* slot_mapping, void* q_out, int64_t q_out_stride_token,
+                               void* k_cache, void* v_cache, int64_t num_blocks, int32_t dtype,
+                               int32_t* err, void* stream);
+
+/* Per row of [n_rows, hidden]: when residual is not NULL, x <- x + residual
+ * (rounded to the element type, in place); then
+ * out = x * rsqrt(mean(x^2) + eps) * weight, computed in fp32 and rounded once.
+ * hidden <= 32768. */
+SEB_API int seb_add_rmsnorm(void* x, int64_t x_stride, const void* residual, int64_t residual_stride,
+                            const void* weight, void* out, int64_t out_stride, int64_t n_rows,
+                            int32_t hidden, float eps, int32_t dtype, void* stream);
+
+/* out[r, f] = silu(gate_up[r, f]) * gate_up[r, ffn + f] for f < ffn, computed in
+ * fp32 and rounded once. */
+SEB_API int seb_swiglu(const void* gate_up, int64_t gate_up_stride, void* out, int64_t out_stride,
+                       int64_t n_rows, int32_t ffn, int32_t dtype, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

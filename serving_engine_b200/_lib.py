@@ -77,6 +77,19 @@ SIGNATURES = {
          c_int32, c_int32, c_int32, c_int32, c_float, c_int32, c_int32,
          c_void_p, c_int64, c_int64, c_void_p, c_int64, c_void_p, c_void_p],
     ),
+    "seb_rope_kv_append": (
+        c_int32,
+        [c_void_p, c_int64, c_int64, c_int32, c_int32, c_int32,  # qkv, stride, n_tokens, hq, hkv, head_dim
+         c_void_p, c_void_p, c_int64,                            # cos, sin, stride
+         c_void_p, c_void_p, c_int64,                            # slot_mapping, q_out, stride
+         c_void_p, c_void_p, c_int64, c_int32, c_void_p, c_void_p],  # k_cache, v_cache, num_blocks, dtype, err, stream
+    ),
+    "seb_add_rmsnorm": (
+        c_int32,
+        [c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_void_p, c_int64, c_int64, c_int32, c_float, c_int32,
+         c_void_p],
+    ),
+    "seb_swiglu": (c_int32, [c_void_p, c_int64, c_void_p, c_int64, c_int64, c_int32, c_int32, c_void_p]),
 }
 NOALLOC_SCRATCH_BYTES = 32 << 20  # SEB_NOALLOC_SCRATCH_BYTES
 

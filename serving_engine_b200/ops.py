@@ -337,3 +337,101 @@ def paged_prefill(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
     LAUNCHES[0] += 1
     _after(dev)
     return out, lse
+
+
+# ------------------------------------------------------ decode-layer fusions
+def _half_dtype(name: str, *tensors: torch.Tensor) -> int:
+    dt = tensors[0].dtype
+    if dt not in (torch.bfloat16, torch.float16) or any(t.dtype != dt for t in tensors):
+        raise ValueError(f"{name}: all tensors must share one dtype, bf16 or fp16")
+    return dtype_code(tensors[0])
+
+
+def rope_kv_append(qkv: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, slot_mapping: torch.Tensor,
+                   k_cache: torch.Tensor, v_cache: torch.Tensor, num_q_heads: int, num_kv_heads: int,
+                   out: torch.Tensor | None = None) -> torch.Tensor:
+    """Rotary embedding fused with the KV write: returns q rotated
+    [n_tokens, num_q_heads, head_dim] and writes rotated K and V of token t to
+    pool slot slot_mapping[t] (one launch).
+
+    qkv: [n_tokens, (num_q_heads + 2 * num_kv_heads) * head_dim] (q heads, then
+    k heads, then v heads); cos/sin: [n_tokens, head_dim] (any leading views that
+    flatten to that, unit stride on head_dim); k_cache/v_cache: [num_blocks, 16,
+    num_kv_heads, head_dim] contiguous. Bit-identical to
+    ``x * cos + rotate_half(x) * sin`` in the element type followed by
+    kv_append.
+    """
+    dev = _require_cuda("rope_kv_append", qkv, cos, sin, slot_mapping, k_cache, v_cache)
+    dt = _half_dtype("rope_kv_append", qkv, cos, sin, k_cache, v_cache)
+    if qkv.dim() != 2 or qkv.stride(1) != 1:
+        raise ValueError("rope_kv_append: qkv must be [n_tokens, width] with unit column stride")
+    n = qkv.shape[0]
+    if k_cache.dim() != 4 or k_cache.shape[1] != BLOCK_SIZE or k_cache.shape[2] != num_kv_heads:
+        raise ValueError(f"rope_kv_append: k_cache must be [num_blocks, {BLOCK_SIZE}, {num_kv_heads}, head_dim]")
+    d = k_cache.shape[3]
+    if qkv.shape[1] != (num_q_heads + 2 * num_kv_heads) * d:
+        raise ValueError(f"rope_kv_append: qkv width {qkv.shape[1]} != ({num_q_heads} + 2 x {num_kv_heads}) x {d}")
+    if v_cache.shape != k_cache.shape or not (k_cache.is_contiguous() and v_cache.is_contiguous()):
+        raise ValueError("rope_kv_append: k_cache and v_cache must be contiguous and of equal shape")
+    cos2, sin2 = cos.reshape(-1, cos.shape[-1]), sin.reshape(-1, sin.shape[-1])
+    if cos2.shape != (n, d) or sin2.shape != (n, d) or cos2.stride() != sin2.stride() or cos2.stride(1) != 1:
+        raise ValueError(f"rope_kv_append: cos and sin must be [n_tokens={n}, head_dim={d}] with equal strides")
+    if slot_mapping.dtype != torch.int64 or slot_mapping.numel() != n:
+        raise ValueError(f"rope_kv_append: slot_mapping must be int64 [{n}]")
+    slot_mapping = slot_mapping.contiguous()
+    if out is None:
+        out = torch.empty(n, num_q_heads, d, dtype=qkv.dtype, device=dev)
+    elif out.shape != (n, num_q_heads, d) or out.stride(2) != 1 or out.stride(1) != d:
+        raise ValueError("rope_kv_append: out must be [n_tokens, num_q_heads, head_dim] with contiguous heads")
+    st = lib().seb_rope_kv_append(qkv.data_ptr(), qkv.stride(0), n, num_q_heads, num_kv_heads, d,
+                                  cos2.data_ptr(), sin2.data_ptr(), cos2.stride(0), slot_mapping.data_ptr(),
+                                  out.data_ptr(), out.stride(0), k_cache.data_ptr(), v_cache.data_ptr(),
+                                  k_cache.shape[0], dt, err_word(dev).data_ptr(), _stream(dev))
+    check("seb_rope_kv_append", st)
+    LAUNCHES[0] += 1
+    _after(dev)
+    return out
+
+
+def add_rmsnorm(x: torch.Tensor, residual: torch.Tensor | None, weight: torch.Tensor, eps: float,
+                out: torch.Tensor | None = None) -> torch.Tensor:
+    """x += residual (in place, when given), then RMSNorm(x) * weight, one launch.
+
+    x, residual, out: [n_rows, hidden] with unit column stride; weight: [hidden].
+    """
+    ts = (x, weight) if residual is None else (x, residual, weight)
+    dev = _require_cuda("add_rmsnorm", *ts)
+    dt = _half_dtype("add_rmsnorm", *ts)
+    if x.dim() != 2 or x.stride(1) != 1 or weight.shape != (x.shape[1],) or not weight.is_contiguous():
+        raise ValueError("add_rmsnorm: x must be [n_rows, hidden] (unit column stride), weight [hidden]")
+    if residual is not None and (residual.shape != x.shape or residual.stride(1) != 1):
+        raise ValueError("add_rmsnorm: residual must match x")
+    if out is None:
+        out = torch.empty_like(x)
+    elif out.shape != x.shape or out.stride(1) != 1 or out.dtype != x.dtype:
+        raise ValueError("add_rmsnorm: out must match x")
+    st = lib().seb_add_rmsnorm(x.data_ptr(), x.stride(0), 0 if residual is None else residual.data_ptr(),
+                               0 if residual is None else residual.stride(0), weight.data_ptr(), out.data_ptr(),
+                               out.stride(0), x.shape[0], x.shape[1], float(eps), dt, _stream(dev))
+    check("seb_add_rmsnorm", st)
+    LAUNCHES[0] += 1
+    _after(dev)
+    return out
+
+
+def swiglu(gate_up: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """silu(gate) * up for gate_up = [gate | up] of shape [n_rows, 2 * ffn], one launch."""
+    dev = _require_cuda("swiglu", gate_up)
+    dt = _half_dtype("swiglu", gate_up)
+    if gate_up.dim() != 2 or gate_up.stride(1) != 1 or gate_up.shape[1] % 2:
+        raise ValueError("swiglu: gate_up must be [n_rows, 2 * ffn] with unit column stride")
+    n, f = gate_up.shape[0], gate_up.shape[1] // 2
+    if out is None:
+        out = torch.empty(n, f, dtype=gate_up.dtype, device=dev)
+    elif out.shape != (n, f) or out.stride(1) != 1 or out.dtype != gate_up.dtype:
+        raise ValueError("swiglu: out must be [n_rows, ffn]")
+    st = lib().seb_swiglu(gate_up.data_ptr(), gate_up.stride(0), out.data_ptr(), out.stride(0), n, f, dt, _stream(dev))
+    check("seb_swiglu", st)
+    LAUNCHES[0] += 1
+    _after(dev)
+    return out

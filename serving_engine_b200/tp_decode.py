@@ -12,6 +12,11 @@ needs no exchange. Embedding and lm_head are replicated.
 Weights are random (seeded per full matrix, then sliced), so every TP degree
 computes the same model. The decode step can be captured in a CUDA graph
 (including the NCCL all-reduces) and replayed with new tokens.
+
+With ``fused=True`` (the default) the layer glue runs as this library's kernels:
+RoPE fused with the KV append, each residual add fused with the following
+RMSNorm, and SwiGLU in one pass; ``fused=False`` runs the same math as eager
+torch ops.
 """
 from __future__ import annotations
 
@@ -51,10 +56,11 @@ class TPLlamaDecoder:
     """Sharded Llama for batched decode at a fixed context (synthetic pre-filled KV)."""
 
     def __init__(self, cfg: TPConfig, rank: int, world: int, device, batch: int, context: int, seed: int = 0,
-                 group=None, fill_kv: bool = True):
+                 group=None, fill_kv: bool = True, fused: bool = True):
         if cfg.kv_heads % world or cfg.heads % world or cfg.ffn % world:
             raise ValueError(f"{world} ranks must divide kv heads {cfg.kv_heads}, heads {cfg.heads}, ffn {cfg.ffn}")
         self.cfg, self.rank, self.world, self.device, self.group = cfg, rank, world, device, group
+        self.fused = fused
         self.batch, self.context = batch, context
         hkv = cfg.kv_heads // world
         hq = cfg.heads // world
@@ -142,6 +148,8 @@ class TPLlamaDecoder:
         return self.logits(tokens).argmax(dim=-1)
 
     def logits(self, tokens: torch.Tensor) -> torch.Tensor:
+        if self.fused:
+            return self._logits_fused(tokens)
         cfg, b, d = self.cfg, self.batch, self.cfg.head_dim
         x = F.embedding(tokens, self.embed)
         for li, w in enumerate(self.layers):
@@ -161,6 +169,26 @@ class TPLlamaDecoder:
             x = x + a
             x = x + self.mlp(F.rms_norm(x, (cfg.hidden,), w["n2"], cfg.eps), w)
         h = F.rms_norm(x, (cfg.hidden,), self.final_norm, cfg.eps)
+        return h @ self.lm_head.t()
+
+    def _logits_fused(self, tokens: torch.Tensor) -> torch.Tensor:
+        """The decode step with the fused layer kernels (same math as the eager path)."""
+        cfg, b, d = self.cfg, self.batch, self.cfg.head_dim
+        x = F.embedding(tokens, self.embed)  # residual stream, updated in place
+        h = ops.add_rmsnorm(x, None, self.layers[0]["n1"], cfg.eps)
+        for li, w in enumerate(self.layers):
+            qkv = h @ w["wqkv"].t()
+            kc, vc = self.kv[li, 0], self.kv[li, 1]
+            q = ops.rope_kv_append(qkv, self.cos, self.sin, self.slots, kc, vc, self.hq, self.hkv)
+            o, _ = ops.paged_decode(q, kc, vc, self.block_table, self.q_starts, self.k_lens, self.q_pos, self.hq,
+                                    self.hkv, self.scale, True)
+            a = o.view(b, self.hq * d) @ w["wo"].t()
+            self._all_reduce(a)
+            h = ops.add_rmsnorm(x, a, w["n2"], cfg.eps)
+            dn = ops.swiglu(h @ w["wgu"].t()) @ w["wd"].t()
+            self._all_reduce(dn)
+            nxt = self.layers[li + 1]["n1"] if li + 1 < len(self.layers) else self.final_norm
+            h = ops.add_rmsnorm(x, dn, nxt, cfg.eps)
         return h @ self.lm_head.t()
 
     def capture(self, warmup: int = 2) -> None:

@@ -76,6 +76,21 @@ def test_prefill_shapes_vs_oracle(dtype, hq, hkv, d):
     assert_close(o, lse, o_ref, lse_ref, dtype)
 
 
+@pytest.mark.parametrize("hq,hkv", [(32, 8), (8, 8), (32, 4), (16, 1)])
+@pytest.mark.parametrize("d", [64, 128])
+def test_prefill_q_tile_pairs(hq, hkv, d):
+    """A CTA computes a pair of Q tiles of 128 // group queries each. Rows whose
+    second tile holds a single query or a ragged tail, pairs that run as two CTAs
+    (early positions, P's remainder) next to pairs that run as one, and a row
+    crossing from the first kind to the second all match the oracle."""
+    qpt = 128 // (hq // hkv)
+    rows = [(qpt + 1, 300), (2 * qpt + 1, 400), (3 * qpt - 5, 260), (300, 100), (2 * qpt, 1000)]
+    b = make_batch(rows, hq, hkv, d, torch.bfloat16, seed=17 + hq + d)
+    o, lse = run_prefill(b)
+    o_ref, lse_ref = oracle(b)
+    assert_close(o, lse, o_ref, lse_ref, torch.bfloat16)
+
+
 def test_prefill_long_chunk_shared_prefix():
     """Config-3 pattern at reduced size: rows share prefix blocks, then prefill a chunk."""
     rows = [(200, 512)] * 4
