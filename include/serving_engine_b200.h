@@ -233,6 +233,13 @@ SEB_API int seb_add_rmsnorm(void* x, int64_t x_stride, const void* residual, int
 SEB_API int seb_swiglu(const void* gate_up, int64_t gate_up_stride, void* out, int64_t out_stride,
                        int64_t n_rows, int32_t ffn, int32_t dtype, void* stream);
 
+/* Self-test of the bounded waits every kernel uses (no counterpart in the
+ * reference, which has no device-side waits): one launch waits `polls` times
+ * (1 .. 2^20) on an mbarrier that nothing arrives on, gives up, sets
+ * SEB_ERRBIT_TIMEOUT in *err and returns; the CUDA context stays usable. It
+ * neither faults nor hangs the GPU. */
+SEB_API int seb_selftest_bounded_wait(uint32_t polls, int32_t* err, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

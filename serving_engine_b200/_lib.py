@@ -8,7 +8,7 @@ from __future__ import annotations
 
 import ctypes
 import os
-from ctypes import POINTER, c_char_p, c_float, c_int32, c_int64, c_void_p
+from ctypes import POINTER, c_char_p, c_float, c_int32, c_int64, c_uint32, c_void_p
 
 from .build import LIB_PATH
 
@@ -90,6 +90,7 @@ SIGNATURES = {
          c_void_p],
     ),
     "seb_swiglu": (c_int32, [c_void_p, c_int64, c_void_p, c_int64, c_int64, c_int32, c_int32, c_void_p]),
+    "seb_selftest_bounded_wait": (c_int32, [c_uint32, c_void_p, c_void_p]),
 }
 NOALLOC_SCRATCH_BYTES = 32 << 20  # SEB_NOALLOC_SCRATCH_BYTES
 

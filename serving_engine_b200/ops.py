@@ -7,6 +7,7 @@ which ``check_device_errors()`` reads back (one sync) and raises on.
 """
 from __future__ import annotations
 
+import functools
 import os
 import threading
 
@@ -30,6 +31,25 @@ _retired_workspaces: list[torch.Tensor] = []
 
 # SEB_DEBUG=1 checks the device error word after every op (one sync per op).
 DEBUG = os.environ.get("SEB_DEBUG", "0") not in ("", "0")
+# SEB_NVTX=1 wraps every op in an NVTX range named "seb.<op>" (for nsys / ncu
+# --nvtx filtering); off, the ops are the plain functions.
+NVTX = os.environ.get("SEB_NVTX", "0") not in ("", "0")
+
+
+def _nvtx(fn):
+    if not NVTX:
+        return fn
+    name = "seb." + fn.__name__
+
+    @functools.wraps(fn)
+    def wrapped(*args, **kwargs):
+        torch.cuda.nvtx.range_push(name)
+        try:
+            return fn(*args, **kwargs)
+        finally:
+            torch.cuda.nvtx.range_pop()
+
+    return wrapped
 
 
 def dtype_code(t: torch.Tensor) -> int:
@@ -96,6 +116,7 @@ def _after(dev: torch.device) -> None:
 
 
 # ------------------------------------------------------------------ kv append
+@_nvtx
 def kv_append(k_new: torch.Tensor, v_new: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
               slot_mapping: torch.Tensor) -> None:
     """k_cache.view(-1, H, D)[slot_mapping] = k_new; same for V (one launch).
@@ -134,6 +155,7 @@ def kv_append(k_new: torch.Tensor, v_new: torch.Tensor, k_cache: torch.Tensor, v
 
 
 # ---------------------------------------------------------------- copy blocks
+@_nvtx
 def copy_blocks(kv_cache: torch.Tensor, src, dst) -> None:
     """kv_cache[:, :, dst] = kv_cache[:, :, src] for the engine pool
     [L, 2, num_blocks, 16, H, D] (model_runner.py:101-110), one launch.
@@ -186,6 +208,7 @@ def decode_workspace_bytes(num_items: int, num_q_heads: int, num_kv_heads: int, 
                                                      max_blocks, blocks_per_split))
 
 
+@_nvtx
 def paged_decode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, block_table: torch.Tensor,
                  q_starts: torch.Tensor, k_lens: torch.Tensor, q_pos_offsets: torch.Tensor,
                  num_q_heads: int, num_kv_heads: int, scale: float, is_causal: bool = True,
@@ -284,6 +307,7 @@ def prefill_supported(q: torch.Tensor, num_q_heads: int, num_kv_heads: int) -> b
             and q.stride(1) >= d and q.stride(0) >= q.stride(1) * num_q_heads)
 
 
+@_nvtx
 def paged_prefill(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, block_table: torch.Tensor,
                   q_starts: torch.Tensor, q_lens: torch.Tensor, k_lens: torch.Tensor, q_pos_offsets: torch.Tensor,
                   num_q_heads: int, num_kv_heads: int, scale: float, is_causal: bool = True, *,
@@ -347,6 +371,7 @@ def _half_dtype(name: str, *tensors: torch.Tensor) -> int:
     return dtype_code(tensors[0])
 
 
+@_nvtx
 def rope_kv_append(qkv: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, slot_mapping: torch.Tensor,
                    k_cache: torch.Tensor, v_cache: torch.Tensor, num_q_heads: int, num_kv_heads: int,
                    out: torch.Tensor | None = None) -> torch.Tensor:
@@ -393,6 +418,7 @@ def rope_kv_append(qkv: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, slot
     return out
 
 
+@_nvtx
 def add_rmsnorm(x: torch.Tensor, residual: torch.Tensor | None, weight: torch.Tensor, eps: float,
                 out: torch.Tensor | None = None) -> torch.Tensor:
     """x += residual (in place, when given), then RMSNorm(x) * weight, one launch.
@@ -419,6 +445,7 @@ def add_rmsnorm(x: torch.Tensor, residual: torch.Tensor | None, weight: torch.Te
     return out
 
 
+@_nvtx
 def swiglu(gate_up: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
     """silu(gate) * up for gate_up = [gate | up] of shape [n_rows, 2 * ffn], one launch."""
     dev = _require_cuda("swiglu", gate_up)
@@ -435,3 +462,13 @@ def swiglu(gate_up: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tens
     LAUNCHES[0] += 1
     _after(dev)
     return out
+
+
+# ------------------------------------------------------------- failure self-test
+def selftest_bounded_wait(polls: int = 4096, device=None) -> None:
+    """Launch the bounded-wait self-test: it waits on an mbarrier nothing arrives
+    on, gives up after `polls` polls and sets SEB_ERRBIT_TIMEOUT in the device's
+    error word (read it with check_device_errors)."""
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    st = lib().seb_selftest_bounded_wait(int(polls), err_word(dev).data_ptr(), _stream(dev))
+    check("seb_selftest_bounded_wait", st)

@@ -89,3 +89,47 @@ def test_tp_mlp_shards_sum_to_full_mlp_gloo():
     ref = full.mlp(h, full.layers[0]).float()
     torch.testing.assert_close(outs[0], ref, atol=2e-3, rtol=2e-2)
     torch.testing.assert_close(outs[0], outs[1], atol=0, rtol=0)  # every rank holds the reduced sum
+
+
+def _leaving_worker(rank, world, port, q):
+    """Rank 1 leaves between steps (exits without joining the next collective);
+    rank 0 must learn of it through its process group's short timeout, as an
+    error from the collective rather than a hang."""
+    import datetime
+    import time
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=3))
+    t = torch.ones(4)
+    dist.all_reduce(t)  # one step together
+    if rank == 1:
+        q.put((rank, "left", float(t[0])))
+        q.close()
+        q.join_thread()  # the message is out before the process goes
+        os._exit(0)  # leave without the next collective or a clean shutdown
+    t0 = time.monotonic()
+    try:
+        dist.all_reduce(t)
+        q.put((rank, "no error", time.monotonic() - t0))
+    except Exception as e:  # noqa: BLE001 - the backend's error type varies
+        q.put((rank, f"error: {type(e).__name__}", time.monotonic() - t0))
+    q.close()
+    q.join_thread()
+    os._exit(0)
+
+
+def test_rank_leaving_ends_peer_collective_with_error():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_leaving_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    outs = dict((r, (msg, v)) for r, msg, v in (q.get(timeout=120) for _ in procs))
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    assert outs[1][0] == "left" and outs[1][1] == 2.0
+    msg, waited = outs[0]
+    assert msg.startswith("error"), msg
+    assert waited < 60, waited
