@@ -44,6 +44,7 @@ struct RopeParams {
   char* v_cache;
   int64_t n_tokens;
   int32_t hq, hkv, d;
+  int32_t pairs;  // 1: 4-byte element-pair accesses are aligned
   int32_t* err;
 };
 
@@ -71,13 +72,45 @@ __global__ void __launch_bounds__(256) rope_append_kernel(RopeParams p) {
     const int h = (r - p.hq) - (is_v ? p.hkv : 0);
     dst = reinterpret_cast<T*>(is_v ? p.v_cache : p.k_cache) + (slot * p.hkv + h) * p.d;
     if (is_v) {
-      for (int i = lane; i < p.d; i += 32) dst[i] = src[i];
+      if (p.pairs) {
+        for (int i = 2 * lane; i < p.d; i += 64)
+          *reinterpret_cast<uint32_t*>(dst + i) = *reinterpret_cast<const uint32_t*>(src + i);
+      } else {
+        for (int i = lane; i < p.d; i += 32) dst[i] = src[i];
+      }
       return;
     }
   }
   const T* cs = reinterpret_cast<const T*>(p.cos + t * p.cs_st);
   const T* sn = reinterpret_cast<const T*>(p.sin + t * p.cs_st);
   const int half = p.d / 2;
+  if (p.pairs) {
+    // element pairs: 4-byte accesses (head_dim % 4 == 0, rows 4-byte aligned)
+    using P2 = uint32_t;
+    for (int i = 2 * lane; i < half; i += 64) {
+      const P2 x1p = *reinterpret_cast<const P2*>(src + i), x2p = *reinterpret_cast<const P2*>(src + i + half);
+      const P2 c1p = *reinterpret_cast<const P2*>(cs + i), c2p = *reinterpret_cast<const P2*>(cs + i + half);
+      const P2 s1p = *reinterpret_cast<const P2*>(sn + i), s2p = *reinterpret_cast<const P2*>(sn + i + half);
+      const T* x1 = reinterpret_cast<const T*>(&x1p);
+      const T* x2 = reinterpret_cast<const T*>(&x2p);
+      const T* c1 = reinterpret_cast<const T*>(&c1p);
+      const T* c2 = reinterpret_cast<const T*>(&c2p);
+      const T* s1 = reinterpret_cast<const T*>(&s1p);
+      const T* s2 = reinterpret_cast<const T*>(&s2p);
+      P2 lo, hi;
+      T* lo_e = reinterpret_cast<T*>(&lo);
+      T* hi_e = reinterpret_cast<T*>(&hi);
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const float a = f32(x1[e]), b = f32(x2[e]);
+        lo_e[e] = Elem<T>::from_float(round_to<T>(a * f32(c1[e])) + round_to<T>(-b * f32(s1[e])));
+        hi_e[e] = Elem<T>::from_float(round_to<T>(b * f32(c2[e])) + round_to<T>(a * f32(s2[e])));
+      }
+      *reinterpret_cast<P2*>(dst + i) = lo;
+      *reinterpret_cast<P2*>(dst + i + half) = hi;
+    }
+    return;
+  }
   for (int i = lane; i < half; i += 32) {
     const float x1 = f32(src[i]), x2 = f32(src[i + half]);
     // rotate_half(x) = (-x2, x1); each product and the sum rounded like the eager ops
@@ -144,6 +177,88 @@ __global__ void __launch_bounds__(256) swiglu_kernel(const T* gu, int64_t gu_st,
   }
 }
 
+// 16-byte vectors of 8 elements.
+template <typename T>
+struct Vec8 {
+  uint4 raw;
+  __device__ __forceinline__ float get(int i) const {
+    return f32(reinterpret_cast<const T*>(&raw)[i]);
+  }
+  __device__ __forceinline__ void set(int i, float v) { reinterpret_cast<T*>(&raw)[i] = Elem<T>::from_float(v); }
+};
+
+// add_rmsnorm_kernel with 16-byte accesses: hidden % 8 == 0 and every row
+// 16-byte aligned; a thread holds up to kMaxVec vectors of its row.
+template <typename T, int THREADS>
+__global__ void __launch_bounds__(THREADS) add_rmsnorm_vec_kernel(T* x, int64_t x_st, const T* a, int64_t a_st,
+                                                                  const T* w, T* out, int64_t o_st, int hidden,
+                                                                  float eps) {
+  constexpr int kMaxVec = 4;
+  __shared__ float red[THREADS / 32];
+  const int64_t row = blockIdx.x;
+  const int nvec = hidden / 8;
+  uint4* xr = reinterpret_cast<uint4*>(x + row * x_st);
+  const uint4* ar = a ? reinterpret_cast<const uint4*>(a + row * a_st) : nullptr;
+  Vec8<T> v[kMaxVec];
+  float ss = 0.f;
+#pragma unroll
+  for (int k = 0; k < kMaxVec; ++k) {
+    const int i = threadIdx.x + k * THREADS;
+    if (i < nvec) {
+      v[k].raw = xr[i];
+      if (ar) {
+        Vec8<T> r;
+        r.raw = ar[i];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) v[k].set(e, v[k].get(e) + r.get(e));  // rounded to T, like the eager add
+        xr[i] = v[k].raw;
+      }
+#pragma unroll
+      for (int e = 0; e < 8; ++e) ss = fmaf(v[k].get(e), v[k].get(e), ss);
+    }
+  }
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  float tot = 0.f;
+#pragma unroll
+  for (int k = 0; k < THREADS / 32; ++k) tot += red[k];
+  const float r = rsqrtf(tot / (float)hidden + eps);
+  uint4* orow = reinterpret_cast<uint4*>(out + row * o_st);
+  const uint4* wv = reinterpret_cast<const uint4*>(w);
+#pragma unroll
+  for (int k = 0; k < kMaxVec; ++k) {
+    const int i = threadIdx.x + k * THREADS;
+    if (i < nvec) {
+      Vec8<T> wk, o;
+      wk.raw = __ldg(wv + i);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) o.set(e, v[k].get(e) * r * wk.get(e));
+      orow[i] = o.raw;
+    }
+  }
+}
+
+// swiglu_kernel with 16-byte accesses: ffn % 8 == 0, rows 16-byte aligned; grid
+// (vector blocks, rows).
+template <typename T>
+__global__ void __launch_bounds__(256) swiglu_vec_kernel(const T* gu, int64_t gu_st, T* out, int64_t o_st, int ffn) {
+  const int64_t row = blockIdx.y;
+  const int i = blockIdx.x * 256 + threadIdx.x;
+  if (i >= ffn / 8) return;
+  const uint4* g4 = reinterpret_cast<const uint4*>(gu + row * gu_st);
+  Vec8<T> g, u, o;
+  g.raw = __ldg(g4 + i);
+  u.raw = __ldg(g4 + ffn / 8 + i);
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    const float gv = g.get(e);
+    o.set(e, gv / (1.f + __expf(-gv)) * u.get(e));
+  }
+  reinterpret_cast<uint4*>(out + row * o_st)[i] = o.raw;
+}
+
 template <typename T, int THREADS>
 void launch_norm(T* x, int64_t x_st, const T* a, int64_t a_st, const T* w, T* out, int64_t o_st, int64_t n, int hidden,
                  float eps, cudaStream_t s) {
@@ -187,6 +302,9 @@ extern "C" int seb_rope_kv_append(const void* qkv, int64_t qkv_stride_token, int
   p.hkv = num_kv_heads;
   p.d = head_dim;
   p.err = err;
+  p.pairs = head_dim % 4 == 0 && aligned(qkv, 4) && aligned(cos, 4) && aligned(sin, 4) && aligned(q_out, 4) &&
+            aligned(k_cache, 4) && aligned(v_cache, 4) && qkv_stride_token % 2 == 0 && cos_sin_stride_token % 2 == 0 &&
+            q_out_stride_token % 2 == 0;
   const int64_t warps = n_tokens * (num_q_heads + 2 * num_kv_heads);
   const int64_t blocks = (warps + 7) / 8;
   SEB_CHECK_ARG(blocks < (1ll << 31), "seb_rope_kv_append: too many tokens");
@@ -210,6 +328,37 @@ extern "C" int seb_add_rmsnorm(void* x, int64_t x_stride, const void* residual, 
   SEB_CHECK_ARG(x && weight && out, "seb_add_rmsnorm: NULL pointer argument");
   SEB_CHECK_ARG(n_rows < (1ll << 31), "seb_add_rmsnorm: too many rows");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const bool vec = hidden % 8 == 0 && hidden <= 4 * 8 * 1024 && aligned(x, 16) && aligned(weight, 16) &&
+                   aligned(out, 16) && (residual == nullptr || aligned(residual, 16)) && x_stride % 8 == 0 &&
+                   out_stride % 8 == 0 && (residual == nullptr || residual_stride % 8 == 0);
+  if (vec) {
+    // up to 4 vectors of 8 per thread: 256 threads up to 8192, 1024 threads above
+    const unsigned grid = (unsigned)n_rows;
+    if (dtype == SEB_BF16) {
+      using T = __nv_bfloat16;
+      if (hidden <= 8192)
+        add_rmsnorm_vec_kernel<T, 256><<<grid, 256, 0, s>>>(static_cast<T*>(x), x_stride, static_cast<const T*>(residual),
+                                                           residual_stride, static_cast<const T*>(weight),
+                                                           static_cast<T*>(out), out_stride, hidden, eps);
+      else
+        add_rmsnorm_vec_kernel<T, 1024><<<grid, 1024, 0, s>>>(static_cast<T*>(x), x_stride,
+                                                             static_cast<const T*>(residual), residual_stride,
+                                                             static_cast<const T*>(weight), static_cast<T*>(out),
+                                                             out_stride, hidden, eps);
+    } else {
+      using T = __half;
+      if (hidden <= 8192)
+        add_rmsnorm_vec_kernel<T, 256><<<grid, 256, 0, s>>>(static_cast<T*>(x), x_stride, static_cast<const T*>(residual),
+                                                           residual_stride, static_cast<const T*>(weight),
+                                                           static_cast<T*>(out), out_stride, hidden, eps);
+      else
+        add_rmsnorm_vec_kernel<T, 1024><<<grid, 1024, 0, s>>>(static_cast<T*>(x), x_stride,
+                                                             static_cast<const T*>(residual), residual_stride,
+                                                             static_cast<const T*>(weight), static_cast<T*>(out),
+                                                             out_stride, hidden, eps);
+    }
+    return launch_status("add_rmsnorm_vec_kernel");
+  }
   // 32 values per thread at most: 256 threads up to 8192, 1024 threads above.
   if (dtype == SEB_BF16) {
     using T = __nv_bfloat16;
@@ -240,9 +389,21 @@ extern "C" int seb_swiglu(const void* gate_up, int64_t gate_up_stride, void* out
   if (n_rows == 0) return SEB_OK;
   SEB_CHECK_ARG(gate_up && out, "seb_swiglu: NULL pointer argument");
   SEB_CHECK_ARG(gate_up_stride >= 2 * (int64_t)ffn && out_stride >= ffn, "seb_swiglu: a row stride is too small");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (ffn % 8 == 0 && aligned(gate_up, 16) && aligned(out, 16) && gate_up_stride % 8 == 0 && out_stride % 8 == 0 &&
+      n_rows <= 65535) {
+    const dim3 grid((unsigned)((ffn / 8 + 255) / 256), (unsigned)n_rows);
+    if (dtype == SEB_BF16)
+      swiglu_vec_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(gate_up),
+                                                             gate_up_stride, static_cast<__nv_bfloat16*>(out),
+                                                             out_stride, ffn);
+    else
+      swiglu_vec_kernel<__half><<<grid, 256, 0, s>>>(static_cast<const __half*>(gate_up), gate_up_stride,
+                                                      static_cast<__half*>(out), out_stride, ffn);
+    return launch_status("swiglu_vec_kernel");
+  }
   const int64_t total = n_rows * (int64_t)ffn;
   const int64_t blocks = std::min<int64_t>((total + 255) / 256, (int64_t)num_sms() * 16);
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (dtype == SEB_BF16)
     swiglu_kernel<__nv_bfloat16><<<(unsigned)blocks, 256, 0, s>>>(
         static_cast<const __nv_bfloat16*>(gate_up), gate_up_stride, static_cast<__nv_bfloat16*>(out), out_stride,

@@ -31,10 +31,12 @@ def rope_tables(pos, d, dtype):
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
 @pytest.mark.parametrize("hq,hkv,d", [(32, 8, 128), (8, 8, 64), (16, 2, 128)])
-def test_rope_kv_append_bit_exact(dtype, hq, hkv, d):
-    g = torch.Generator(device=DEV).manual_seed(hq * d)
+@pytest.mark.parametrize("offset", [0, 1])  # 1: a 2-byte-offset view takes the element-at-a-time path
+def test_rope_kv_append_bit_exact(dtype, hq, hkv, d, offset):
+    g = torch.Generator(device=DEV).manual_seed(hq * d + offset)
     n, nb = 37, 20
-    qkv = torch.randn(n, (hq + 2 * hkv) * d, generator=g, device=DEV).to(dtype)
+    w = (hq + 2 * hkv) * d
+    qkv = torch.randn(n, w + 2, generator=g, device=DEV).to(dtype)[:, offset:offset + w]
     pos = torch.randint(0, 4000, (n,), generator=g, device=DEV)
     cos, sin = rope_tables(pos, d, dtype)
     slots = torch.randperm(nb * 16, generator=g, device=DEV)[:n]
@@ -77,7 +79,7 @@ def assert_within_ulp(out, ref32):
 
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
-@pytest.mark.parametrize("n,hidden", [(256, 4096), (3, 2048), (5, 10000)])
+@pytest.mark.parametrize("n,hidden", [(256, 4096), (3, 2048), (5, 10000), (4, 1001)])
 def test_add_rmsnorm(dtype, n, hidden):
     g = torch.Generator(device=DEV).manual_seed(hidden + n)
     x = torch.randn(n, hidden, generator=g, device=DEV).to(dtype)
@@ -96,9 +98,10 @@ def test_add_rmsnorm(dtype, n, hidden):
 
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
-def test_swiglu(dtype):
+@pytest.mark.parametrize("ffn", [1792, 1001])  # 1001: the element-at-a-time path
+def test_swiglu(dtype, ffn):
     g = torch.Generator(device=DEV).manual_seed(3)
-    gu = (2 * torch.randn(77, 2 * 1792, generator=g, device=DEV)).to(dtype)
+    gu = (2 * torch.randn(77, 2 * ffn, generator=g, device=DEV)).to(dtype)
     out = ops.swiglu(gu)
     torch.cuda.synchronize()
     f = gu.shape[1] // 2
