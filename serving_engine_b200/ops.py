@@ -221,6 +221,10 @@ def paged_decode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, 
     block_table int32 [rows, max_blocks]; q_starts/k_lens/q_pos_offsets int32 [rows].
     Returns (out like q, lse fp32 [total_query, num_q_heads]); rows of tokens that
     are not items are left untouched.
+
+    The split-K scratch is one workspace per device, shared by every call on that
+    device: calls on different streams must not run at the same time (calls in
+    stream order, or inside one CUDA graph, are fine).
     """
     dev = _require_cuda("paged_decode", q, k_cache, v_cache, block_table, q_starts, k_lens, q_pos_offsets)
     if q.dim() != 3 or q.stride(2) != 1:
