@@ -67,7 +67,7 @@ struct DecodeParams {
   int64_t lse_st;
   float* ws_o;   // [items][hq][max_splits][D]
   float* ws_ml;  // [items][hq][max_splits][2]  (m in log2 units, l)
-  int32_t* counters;  // [items][hkv] splits finished; zero between calls
+  int32_t* counters;  // [items][hkv] splits finished; cleared before each launch
   int32_t* err;
 };
 
