@@ -102,8 +102,11 @@ class PackedMetadata:
         else:
             self.max_block_id = -1
         a[o_items:o_items + total_query] = np.repeat(np.arange(rows, dtype=np.int32), q_lens_np)
-        # decode items (rows with q_len == 1: token, row) and prefill rows (q_len > 1)
+        # decode items (rows with q_len == 1: token, row) and prefill rows (q_len > 1).
+        # Decode items go longest context first: the kernel's work is dispatched in
+        # item order, so the short items fill the tail.
         dec_rows = np.nonzero(q_lens_np == 1)[0].astype(np.int32)
+        dec_rows = dec_rows[np.argsort(-np.asarray(k_lens, dtype=np.int64).reshape(rows)[dec_rows], kind="stable")]
         pre_rows = np.nonzero(q_lens_np > 1)[0].astype(np.int32)
         starts_np = a[2 * rows:3 * rows]
         o_dec = o_items + total_query
