@@ -58,6 +58,8 @@ def parse_args():
     ap.add_argument("--tp-batch", type=int, default=256)
     ap.add_argument("--tp-context", type=int, default=4096)
     ap.add_argument("--no-graph", action="store_true", help="tp / e2e: run decode steps eagerly")
+    ap.add_argument("--tp-allreduce", default="peer", choices=["peer", "nccl"],
+                    help="tp: all-reduce + add + RMSNorm as one peer-memory kernel, or NCCL then the norm kernel")
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--batch", type=int, default=64)
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -574,7 +576,7 @@ def run_tp_workload(args, rank, world, device, dist):
     from serving_engine_b200.tp_decode import LLAMA3_8B, TPLlamaDecoder
 
     dec = TPLlamaDecoder(LLAMA3_8B, rank, world, device, batch=args.tp_batch, context=args.tp_context,
-                         seed=args.seed)
+                         seed=args.seed, allreduce=args.tp_allreduce)
     graph = not args.no_graph
     if graph:
         dec.capture(warmup=2)
@@ -604,7 +606,8 @@ def run_tp_workload(args, rank, world, device, dist):
         "data": "synthetic (random-init weights, random pre-filled KV)",
         "config": {"workload": "config 5: Llama-3-8B shape, decode batch 256 at 4096 context",
                    "batch": args.tp_batch, "context": args.tp_context, "parallelism": f"tp{world} (kv-head shard)",
-                   "cuda_graph": graph, "all_reduces_per_step": 2 * LLAMA3_8B.layers if world > 1 else 0},
+                   "cuda_graph": graph, "all_reduces_per_step": 2 * LLAMA3_8B.layers if world > 1 else 0,
+                   "all_reduce": dec.allreduce if world > 1 else None},
         "hbm_bytes_per_step_per_gpu": per_gpu_bytes,
         "roofline": {"bound": "hbm", "achieved": round(per_gpu_bytes / (ms * 1e-3) / 1e9, 1), "unit": "GB/s",
                      "peak": peaks()[0], "frac": round(per_gpu_bytes / (ms * 1e-3) / 1e9 / peaks()[0], 4),

@@ -30,6 +30,7 @@
 #ifndef SERVING_ENGINE_B200_H
 #define SERVING_ENGINE_B200_H
 
+#include <stddef.h>
 #include <stdint.h>
 
 #ifdef __cplusplus
@@ -232,6 +233,48 @@ SEB_API int seb_add_rmsnorm(void* x, int64_t x_stride, const void* residual, int
  * fp32 and rounded once. */
 SEB_API int seb_swiglu(const void* gate_up, int64_t gate_up_stride, void* out, int64_t out_stride,
                        int64_t n_rows, int32_t ffn, int32_t dtype, void* stream);
+
+/* ------------------------------------------------------------------------
+ * All-reduce fused with the residual add + RMSNorm that follows it in the
+ * tensor-parallel decoder (after o_proj and after down_proj), over CUDA IPC
+ * peer memory. New: the reference runs on one GPU; this replaces
+ * torch.distributed.all_reduce(SUM) of the [n_tokens, hidden] partial sums
+ * followed by seb_add_rmsnorm.
+ *
+ * Peer memory: seb_peer_alloc returns zeroed device memory (cudaMalloc) whose
+ * handle (SEB_PEER_HANDLE_BYTES, from seb_peer_export) another process opens
+ * with seb_peer_import (CUDA IPC, peer access enabled). Close imported
+ * pointers (seb_peer_close) on every rank before the owner frees them.
+ * ------------------------------------------------------------------------ */
+#define SEB_MAX_PEERS 8
+#define SEB_PEER_HANDLE_BYTES 64
+#define SEB_PEER_FLAG_BYTES 1024 /* flag words of one rank, zero before the first call */
+
+SEB_API int seb_peer_alloc(size_t bytes, void** ptr);
+SEB_API int seb_peer_free(void* ptr);
+SEB_API int seb_peer_export(void* ptr, void* handle);
+SEB_API int seb_peer_import(const void* handle, void** ptr);
+SEB_API int seb_peer_close(void* ptr);
+
+/* partial, x, out, flags: host arrays of `world` device pointers, rank q's
+ * buffers as mapped on this device (this rank's own and the imported ones):
+ * partial[q] and x[q], out[q] are contiguous [n_tokens, hidden], flags[q] is
+ * SEB_PEER_FLAG_BYTES. For every token row t, with S the sum over ranks of
+ * partial[q][t] (fp32 in rank order, rounded once to the element type: the
+ * all-reduce result), every rank's x[t] becomes x[t] + S (rounded) and its
+ * out[t] the RMSNorm of that row times `weight`, computed as seb_add_rmsnorm
+ * computes it. Rank r computes rows [r*n_tokens/world, (r+1)*n_tokens/world)
+ * and stores them on every rank. Each rank issues one call per all-reduce, in
+ * the same order on every rank (CUDA-graph capturable: the call count is kept
+ * in the flag words). all_ranks = 1 (rank 0) runs every rank's part in one
+ * cooperative launch on this device, all buffers being on it. `polls` bounds
+ * every wait for a peer (0: a default of a few seconds); a wait that gives up
+ * sets SEB_ERRBIT_TIMEOUT in *err and the call returns with invalid rows.
+ * hidden % 8 == 0, <= 32768; buffers and weight 16-byte aligned. */
+SEB_API int seb_allreduce_add_rmsnorm(void* const* partial, void* const* x, void* const* out, void* const* flags,
+                                      const void* weight, int64_t n_tokens, int32_t hidden, float eps,
+                                      int32_t dtype, int32_t rank, int32_t world, int32_t all_ranks,
+                                      uint32_t polls, int32_t* err, void* stream);
 
 /* Self-test of the bounded waits every kernel uses (no counterpart in the
  * reference, which has no device-side waits): one launch waits `polls` times

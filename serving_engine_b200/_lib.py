@@ -8,7 +8,7 @@ from __future__ import annotations
 
 import ctypes
 import os
-from ctypes import POINTER, c_char_p, c_float, c_int32, c_int64, c_uint32, c_void_p
+from ctypes import POINTER, c_char_p, c_float, c_int32, c_int64, c_size_t, c_uint32, c_void_p
 
 from .build import LIB_PATH
 
@@ -91,7 +91,22 @@ SIGNATURES = {
     ),
     "seb_swiglu": (c_int32, [c_void_p, c_int64, c_void_p, c_int64, c_int64, c_int32, c_int32, c_void_p]),
     "seb_selftest_bounded_wait": (c_int32, [c_uint32, c_void_p, c_void_p]),
+    "seb_peer_alloc": (c_int32, [c_size_t, POINTER(c_void_p)]),
+    "seb_peer_free": (c_int32, [c_void_p]),
+    "seb_peer_export": (c_int32, [c_void_p, c_void_p]),
+    "seb_peer_import": (c_int32, [c_void_p, POINTER(c_void_p)]),
+    "seb_peer_close": (c_int32, [c_void_p]),
+    "seb_allreduce_add_rmsnorm": (
+        c_int32,
+        [c_void_p, c_void_p, c_void_p, c_void_p,  # partial, x, out, flags (host arrays of device pointers)
+         c_void_p, c_int64, c_int32, c_float,     # weight, n_tokens, hidden, eps
+         c_int32, c_int32, c_int32, c_int32,      # dtype, rank, world, all_ranks
+         c_uint32, c_void_p, c_void_p],           # polls, err, stream
+    ),
 }
+SEB_MAX_PEERS = 8
+SEB_PEER_HANDLE_BYTES = 64
+SEB_PEER_FLAG_BYTES = 1024
 NOALLOC_SCRATCH_BYTES = 32 << 20  # SEB_NOALLOC_SCRATCH_BYTES
 
 _LIB: ctypes.CDLL | None = None

@@ -15,6 +15,7 @@
 // Roofline: HBM (a few MB per call); at decode sizes these are launch-latency
 // bound, which is what fusing them saves.
 #include "seb_common.cuh"
+#include "seb_vec.cuh"
 
 #include <algorithm>
 
@@ -177,16 +178,6 @@ __global__ void __launch_bounds__(256) swiglu_kernel(const T* gu, int64_t gu_st,
   }
 }
 
-// 16-byte vectors of 8 elements.
-template <typename T>
-struct Vec8 {
-  uint4 raw;
-  __device__ __forceinline__ float get(int i) const {
-    return f32(reinterpret_cast<const T*>(&raw)[i]);
-  }
-  __device__ __forceinline__ void set(int i, float v) { reinterpret_cast<T*>(&raw)[i] = Elem<T>::from_float(v); }
-};
-
 // add_rmsnorm_kernel with 16-byte accesses: hidden % 8 == 0 and every row
 // 16-byte aligned; a thread holds up to kMaxVec vectors of its row.
 template <typename T, int THREADS>
@@ -200,7 +191,6 @@ __global__ void __launch_bounds__(THREADS) add_rmsnorm_vec_kernel(T* x, int64_t 
   uint4* xr = reinterpret_cast<uint4*>(x + row * x_st);
   const uint4* ar = a ? reinterpret_cast<const uint4*>(a + row * a_st) : nullptr;
   Vec8<T> v[kMaxVec];
-  float ss = 0.f;
 #pragma unroll
   for (int k = 0; k < kMaxVec; ++k) {
     const int i = threadIdx.x + k * THREADS;
@@ -213,18 +203,9 @@ __global__ void __launch_bounds__(THREADS) add_rmsnorm_vec_kernel(T* x, int64_t 
         for (int e = 0; e < 8; ++e) v[k].set(e, v[k].get(e) + r.get(e));  // rounded to T, like the eager add
         xr[i] = v[k].raw;
       }
-#pragma unroll
-      for (int e = 0; e < 8; ++e) ss = fmaf(v[k].get(e), v[k].get(e), ss);
     }
   }
-#pragma unroll
-  for (int off = 16; off >= 1; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
-  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
-  __syncthreads();
-  float tot = 0.f;
-#pragma unroll
-  for (int k = 0; k < THREADS / 32; ++k) tot += red[k];
-  const float r = rsqrtf(tot / (float)hidden + eps);
+  const float r = rms_scale<T, THREADS, kMaxVec>(v, nvec, hidden, eps, red);
   uint4* orow = reinterpret_cast<uint4*>(out + row * o_st);
   const uint4* wv = reinterpret_cast<const uint4*>(w);
 #pragma unroll

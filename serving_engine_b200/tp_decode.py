@@ -16,7 +16,11 @@ computes the same model. The decode step can be captured in a CUDA graph
 With ``fused=True`` (the default) the layer glue runs as this library's kernels:
 RoPE fused with the KV append, each residual add fused with the following
 RMSNorm, and SwiGLU in one pass; ``fused=False`` runs the same math as eager
-torch ops.
+torch ops. With ``allreduce="peer"`` (fused only, world > 1) each all-reduce
+and the residual add + RMSNorm after it are one kernel over CUDA IPC peer
+memory (``PeerAllReduceNorm``) instead of NCCL followed by the add + norm
+kernel: o_proj and down_proj write their partial sums straight into this
+rank's peer buffer, and the residual stream lives there too.
 """
 from __future__ import annotations
 
@@ -56,11 +60,14 @@ class TPLlamaDecoder:
     """Sharded Llama for batched decode at a fixed context (synthetic pre-filled KV)."""
 
     def __init__(self, cfg: TPConfig, rank: int, world: int, device, batch: int, context: int, seed: int = 0,
-                 group=None, fill_kv: bool = True, fused: bool = True):
+                 group=None, fill_kv: bool = True, fused: bool = True, allreduce: str = "nccl"):
         if cfg.kv_heads % world or cfg.heads % world or cfg.ffn % world:
             raise ValueError(f"{world} ranks must divide kv heads {cfg.kv_heads}, heads {cfg.heads}, ffn {cfg.ffn}")
+        if allreduce not in ("nccl", "peer") or (allreduce == "peer" and not fused):
+            raise ValueError(f"allreduce must be 'nccl' or 'peer' (peer needs fused=True), got {allreduce!r}")
         self.cfg, self.rank, self.world, self.device, self.group = cfg, rank, world, device, group
         self.fused = fused
+        self.allreduce = allreduce if world > 1 else "nccl"  # one rank: nothing to reduce
         self.batch, self.context = batch, context
         hkv = cfg.kv_heads // world
         hq = cfg.heads // world
@@ -124,6 +131,11 @@ class TPLlamaDecoder:
         self.scale = 1.0 / math.sqrt(d)
         self.tokens = torch.zeros(batch, dtype=torch.int64, device=device)
         self.graph = None
+        self.ar = None
+        if self.allreduce == "peer":
+            from .peer_allreduce import PeerAllReduceNorm
+
+            self.ar = PeerAllReduceNorm(batch, cfg.hidden, torch.bfloat16, device, group)
 
     def _all_reduce(self, x: torch.Tensor) -> None:
         if self.world > 1:
@@ -173,6 +185,8 @@ class TPLlamaDecoder:
 
     def _logits_fused(self, tokens: torch.Tensor) -> torch.Tensor:
         """The decode step with the fused layer kernels (same math as the eager path)."""
+        if self.ar is not None:
+            return self._logits_peer(tokens)
         cfg, b, d = self.cfg, self.batch, self.cfg.head_dim
         x = F.embedding(tokens, self.embed)  # residual stream, updated in place
         h = ops.add_rmsnorm(x, None, self.layers[0]["n1"], cfg.eps)
@@ -189,6 +203,25 @@ class TPLlamaDecoder:
             self._all_reduce(dn)
             nxt = self.layers[li + 1]["n1"] if li + 1 < len(self.layers) else self.final_norm
             h = ops.add_rmsnorm(x, dn, nxt, cfg.eps)
+        return h @ self.lm_head.t()
+
+    def _logits_peer(self, tokens: torch.Tensor) -> torch.Tensor:
+        """The fused decode step with each all-reduce + add + RMSNorm as one
+        peer-memory kernel; the residual stream is ``self.ar.x``."""
+        cfg, b, d, ar = self.cfg, self.batch, self.cfg.head_dim, self.ar
+        torch.index_select(self.embed, 0, tokens, out=ar.x)
+        h = ops.add_rmsnorm(ar.x, None, self.layers[0]["n1"], cfg.eps)
+        for li, w in enumerate(self.layers):
+            qkv = h @ w["wqkv"].t()
+            kc, vc = self.kv[li, 0], self.kv[li, 1]
+            q = ops.rope_kv_append(qkv, self.cos, self.sin, self.slots, kc, vc, self.hq, self.hkv)
+            o, _ = ops.paged_decode(q, kc, vc, self.block_table, self.q_starts, self.k_lens, self.q_pos, self.hq,
+                                    self.hkv, self.scale, True)
+            torch.mm(o.view(b, self.hq * d), w["wo"].t(), out=ar.partial)
+            h = ar(w["n2"], cfg.eps)
+            torch.mm(ops.swiglu(h @ w["wgu"].t()), w["wd"].t(), out=ar.partial)
+            nxt = self.layers[li + 1]["n1"] if li + 1 < len(self.layers) else self.final_norm
+            h = ar(nxt, cfg.eps)
         return h @ self.lm_head.t()
 
     def capture(self, warmup: int = 2) -> None:
@@ -213,6 +246,10 @@ class TPLlamaDecoder:
             self.tokens.copy_(self.forward(self.tokens))
 
     def release(self) -> None:
-        """Drop the CUDA graph (it holds NCCL work) before the process group goes away."""
+        """Drop the CUDA graph (it holds NCCL work) and the peer buffers
+        (collective) before the process group goes away."""
         self.graph = None
         self.out_tokens = None
+        if self.ar is not None:
+            self.ar.close()
+            self.ar = None
