@@ -103,6 +103,8 @@ class TPLlamaDecoder:
         # KV pool shard: every sequence owns ceil(context / 16) blocks; the
         # current token is appended at position context - 1 each step.
         self.blocks_per_seq = math.ceil(context / BLOCK_SIZE)
+        self.bps = (ops.decode_blocks_per_split(batch, hkv, self.blocks_per_seq, device)
+                    if torch.device(device).type == "cuda" else 0)
         nb = batch * self.blocks_per_seq
         self.kv = torch.empty(cfg.layers, 2, nb, BLOCK_SIZE, hkv, d, dtype=torch.bfloat16, device=device)
         if fill_kv:
@@ -175,7 +177,7 @@ class TPLlamaDecoder:
             kc, vc = self.kv[li, 0], self.kv[li, 1]
             ops.kv_append(k, v, kc, vc, self.slots)
             o, _ = ops.paged_decode(q, kc, vc, self.block_table, self.q_starts, self.k_lens, self.q_pos, self.hq,
-                                    self.hkv, self.scale, True)
+                                    self.hkv, self.scale, True, blocks_per_split=self.bps)
             a = o.view(b, self.hq * d) @ w["wo"].t()
             self._all_reduce(a)
             x = x + a
@@ -195,7 +197,7 @@ class TPLlamaDecoder:
             kc, vc = self.kv[li, 0], self.kv[li, 1]
             q = ops.rope_kv_append(qkv, self.cos, self.sin, self.slots, kc, vc, self.hq, self.hkv)
             o, _ = ops.paged_decode(q, kc, vc, self.block_table, self.q_starts, self.k_lens, self.q_pos, self.hq,
-                                    self.hkv, self.scale, True)
+                                    self.hkv, self.scale, True, blocks_per_split=self.bps)
             a = o.view(b, self.hq * d) @ w["wo"].t()
             self._all_reduce(a)
             h = ops.add_rmsnorm(x, a, w["n2"], cfg.eps)
@@ -216,7 +218,7 @@ class TPLlamaDecoder:
             kc, vc = self.kv[li, 0], self.kv[li, 1]
             q = ops.rope_kv_append(qkv, self.cos, self.sin, self.slots, kc, vc, self.hq, self.hkv)
             o, _ = ops.paged_decode(q, kc, vc, self.block_table, self.q_starts, self.k_lens, self.q_pos, self.hq,
-                                    self.hkv, self.scale, True)
+                                    self.hkv, self.scale, True, blocks_per_split=self.bps)
             torch.mm(o.view(b, self.hq * d), w["wo"].t(), out=ar.partial)
             h = ar(w["n2"], cfg.eps)
             torch.mm(ops.swiglu(h @ w["wgu"].t()), w["wd"].t(), out=ar.partial)
