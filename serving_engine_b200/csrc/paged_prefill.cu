@@ -6,31 +6,33 @@
 // runs 16x16 tiles per (q tile, row, q head) and reads the KV of a kv head once
 // per q head of its GQA group.
 //
-// One CTA computes two 128-row Q tiles of one prefill row and one kv head; the
-// 128 MMA rows of a Q tile pack (query, head) pairs of the GQA group, row
-// m = query (m / G), head (m % G), so each K/V tile is read once for the whole
-// group and feeds 256 rows. K/V tiles hold 64 keys (4 paged blocks).
-//   warp 0     TMA producer: the two Q tiles once, then K and V tiles gathered
-//              through the block table (block ids prefetched a window ahead)
-//              into 3-stage rings of 128B-swizzled panels; K runs three tiles
-//              ahead of V, matching the order the MMAs consume them;
-//   warp 1     owns TMEM (512 columns: two S buffers of 64 columns and one O
-//              accumulator per Q tile) and issues the MMAs from one thread:
-//              per KV tile j, O(t) += P(t, j) V(j) for both Q tiles, then
-//              S(t, j+2) = Q(t) K(j+2)^T, so the next scores are always ready;
+// Two kernels share the work-unit definition: a unit is one prefill row, one kv
+// head and a pair of 128-row Q tiles (256 MMA rows). The 128 MMA rows of a Q
+// tile pack (query, head) pairs of the GQA group, row m = query (m / G), head
+// (m % G), so each K/V tile is read once for the whole group. K/V tiles hold
+// 128 keys (8 paged blocks), gathered through the block table by TMA as 16-row
+// boxes of 128-byte panels.
+//
+// prefill_pair_kernel (head_dim 128) runs a unit on a cluster of two CTAs whose
+// MMAs span both SMs (tcgen05 cta_group::2); it is described above the kernel.
+//
+// prefill_tc_kernel (head_dim 64) runs a unit in one CTA:
+//   warp 0     TMA producer: the Q tiles once, then K and V tiles (block ids
+//              prefetched a window ahead) into 2-stage rings;
+//   warp 1     owns TMEM (512 columns: per Q tile, S of 128 columns with P
+//              written over its first 64 as 16-bit pairs, and O) and issues the
+//              MMAs from one thread in ping-pong order: per KV tile j and Q tile
+//              t, O(t) += P(t, j) V(j) (P read from TMEM), then S(t, j + 1),
+//              so one Q tile's softmax runs while the other's MMAs execute;
 //   warps 2-9  one softmax warpgroup per Q tile; a thread owns one tile row
-//              (TMEM lane): read its 64 scores, mask boundary tiles, online
-//              softmax with a lazily rescaled reference max (O and l are only
-//              rescaled when a block max exceeds it by 2^8), write P as bf16 to
-//              a swizzled shared-memory tile (double-buffered, so P(j+1) is
-//              written while PV(j) runs), and finally normalise its row of O,
-//              store it and the LSE.
-// Two Q tiles per K/V tile halve the TMA traffic per FLOP: a paged K/V tile is
-// 16-row boxes (one per block and 128-byte panel), whose per-SM TMA rate, not
-// L2 bandwidth, bounds a one-Q-tile design.
-// P V is split into a 16-bit high part and its 16-bit remainder for CTAs
-// whose first row sees fewer than kSplitBelow keys (early positions of a
-// prompt), where one rounding of P would cost more than the output tolerance.
+//              (TMEM lane): read its 128 scores in one TMEM round trip, mask
+//              boundary tiles, online softmax with a lazily rescaled reference
+//              max (O and l are only rescaled when a block max exceeds it by
+//              2^8), write P, and finally normalise its row of O, store it and
+//              the LSE.
+// P V is split into a 16-bit high part and its 16-bit remainder for units whose
+// first query sees fewer than kSplitBelow keys (early positions of a prompt),
+// where one rounding of P would cost more than the output tolerance.
 //
 // Roofline: tensor. Algorithmic FLOPs per call = sum over rows, heads and
 // queries of 4 * head_dim * (visible keys of that query).
@@ -38,6 +40,7 @@
 #include "seb_tcgen05.cuh"
 #include "seb_tma.cuh"
 
+#include <algorithm>
 #include <type_traits>
 
 namespace seb {
@@ -110,6 +113,11 @@ enum {
   kNumBars = 16
 };
 
+// Barrier `id` (1..15) over `n` threads (a multiple of 32) of the CTA.
+__device__ __forceinline__ void named_bar_sync(int id, int n) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
+}
+
 // 2^x by the MUFU instruction (ex2.approx.ftz: 2^-22 relative error, -inf -> +0).
 __device__ __forceinline__ float fast_exp2(float x) {
   float y;
@@ -124,6 +132,17 @@ __device__ __forceinline__ bool wait_or_flag(uint32_t bar, uint32_t parity, bool
     return false;
   }
   return true;
+}
+
+// The same for the CTA-pair kernel, whose barriers are completed from the
+// other SM of the pair: short suspensions, bounded at about one second.
+__device__ __forceinline__ bool wait_or_flag_cluster(uint32_t bar, uint32_t parity, bool& failed) {
+  if (failed) return false;
+  if (mbar_test_wait(bar, parity)) return true;
+  for (uint32_t i = 0; i < (1u << 23); ++i)
+    if (mbar_try_wait_hint(bar, parity, 128)) return true;
+  failed = true;
+  return false;
 }
 
 // Scores of keys [key0, key0 + 32) of one row, masked in place when the tile is
@@ -532,6 +551,540 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+// ---------------------------------------------------------------------------
+// CTA-pair kernel (head_dim 128). A cluster of two CTAs on two SMs computes
+// the 256 MMA rows of a pair of Q tiles with every MMA spanning both SMs
+// (tcgen05 cta_group::2, M = 256): CTA r holds Q rows [128 r, 128 r + 128) and
+// their S and O in its own TMEM; of each 128-key tile it loads half of K (keys
+// [64 r, 64 r + 64)) and half of V (head dims [64 r, 64 r + 64)). Per SM that
+// halves the operand bytes the tensor core reads from shared memory for 128 MMA
+// rows, and it frees TMEM for three S buffers per SM: S(j + 3) is issued as soon
+// as P V(j) has released its buffer, so the softmax finds its next scores ready
+// and runs back to back.
+// The kernel is persistent: one cluster per SM pair walks the work units
+// (prefill row, kv head, pair of Q tiles) c, c + C, c + 2C, ... with its K/V
+// rings, S buffers and their barrier phases running on from unit to unit, and Q
+// double-buffered, so the next unit's Q and first K/V tiles load while the
+// current unit finishes.
+//   warp 0     TMA producer of its CTA's Q tile and K halves; warp 10 of its V
+//              halves. Both complete their bytes on the even CTA's barriers;
+//   warp 11    (even CTA) issues S(j) once K(j) landed and P V(j - 3) released
+//              S buffer j % 3; warp 1 (even CTA) issues P V(j) once V(j) landed
+//              and both CTAs wrote P(j). Their commits arrive on both CTAs';
+//   warps 2-9  softmax of the CTA's 128 rows in two warpgroups, one per half
+//              (64 keys) of a tile, so two warps share each sub-partition: a
+//              thread owns one row of its half, the halves exchange row maxima
+//              through shared memory, P goes over the buffer's first 64 columns
+//              and, for pairs whose first query sees fewer than kSplitBelow
+//              keys, P's 16-bit remainder over the next 64 (read already).
+constexpr int kPairThreads = 384;
+constexpr int kPairVWarp = 10;   // V producer
+constexpr int kPairSWarp = 11;   // S = Q K^T issuer
+constexpr int kPairKStages = 3;
+constexpr int kPairVStages = 4;
+constexpr int kPairColO = 384;   // O: columns [384, 512); S buffer b: [128 b, 128 b + 128)
+
+struct PairLayout {
+  static constexpr int kPanelQ = 128 * 128;    // 128 rows x 128 bytes
+  static constexpr int kTileQ = 2 * kPanelQ;   // 128 rows x 128 dims
+  static constexpr int kPanelK = 64 * 128;     // 64 keys x 128 bytes
+  static constexpr int kStageK = 2 * kPanelK;  // 64 keys x 128 dims
+  static constexpr int kStageV = 128 * 128;    // 128 keys x 64 dims
+  static constexpr int oQ = 0;                 // [2 buffers]
+  static constexpr int oK = oQ + 2 * kTileQ;
+  static constexpr int oV = oK + kPairKStages * kStageK;
+  static constexpr int oBar = oV + kPairVStages * kStageV;
+  static constexpr int oX = oBar + 512;        // [tile parity][half][row] row maxima; row sums at unit ends
+  static constexpr int kBytes = oX + 2 * 2 * 128 * 4;
+};
+
+enum {
+  kPBarQFull = 0,                              // +buffer (2), even CTA: both Q halves landed
+  kPBarQEmpty = 2,                             // +buffer, both CTAs: the unit's last S done
+  kPBarKFull = 4,                              // +stage (3), even CTA: both K halves landed
+  kPBarKEmpty = kPBarKFull + kPairKStages,     // +stage, both CTAs: S of the tile done
+  kPBarVFull = kPBarKEmpty + kPairKStages,     // +stage (4), even CTA: two arrivals (one per CTA)
+  kPBarVEmpty = kPBarVFull + kPairVStages,     // +stage, both CTAs
+  kPBarSFull = kPBarVEmpty + kPairVStages,     // +buffer (3), both CTAs
+  kPBarPFull = kPBarSFull + 3,                 // +buffer, even CTA: 16 softmax warps wrote P
+  kPBarPFree = kPBarPFull + 3,                 // +buffer, both CTAs: P V of the buffer done
+  kPBarDone = kPBarPFree + 3,                  // both CTAs: a final commit of each issuing warp
+  kPBarVLand = kPBarDone + 1,                  // local: this CTA's V half of a unit's last tile landed
+  kPNumBars = kPBarVLand + 1
+};
+static_assert(kPNumBars * 8 + 16 <= 512, "barrier region");
+
+// One work unit of the pair kernel, decoded identically by every role of both CTAs.
+struct PairUnit {
+  int row, kvh, q_len, q_start, k_len, qpos0, ceil16, pair0, i_last, nblk, ntiles;
+  bool split;
+};
+
+// Decodes unit u; false: the unit does nothing (no such row or pair).
+__device__ __forceinline__ bool pair_unit(const PrefillParams& p, int u, PairUnit& w) {
+  const int pr = p.mpairs - 1 - (u % p.mpairs);
+  u /= p.mpairs;
+  w.kvh = u % p.hkv;
+  const int prow = u / p.hkv;
+  if (prow >= p.num_prefill_rows) return false;
+  w.row = p.rows ? __ldg(p.rows + prow) : prow;
+  if (w.row < 0 || w.row >= p.num_rows) return false;
+  w.q_len = __ldg(p.q_lens + w.row);
+  w.q_start = __ldg(p.q_starts + w.row);
+  w.k_len = max(__ldg(p.k_lens + w.row), 0);
+  w.qpos0 = __ldg(p.q_pos + w.row);
+  w.ceil16 = (w.k_len + 15) & ~15;
+  w.pair0 = pr * 2 * p.qpt;
+  if (w.pair0 >= w.q_len) return false;
+  w.i_last = min(w.pair0 + 2 * p.qpt, w.q_len) - 1;
+  w.split = (p.causal ? min(w.ceil16, w.qpos0 + w.pair0 + 1) : w.ceil16) < kSplitBelow;
+  const int nvis = max(p.causal ? min(w.ceil16, w.qpos0 + w.i_last + 1) : w.ceil16, 0);
+  w.nblk = min((nvis + 15) >> 4, (int)p.max_blocks);
+  w.ntiles = (w.nblk + 7) >> 3;
+  return true;
+}
+
+template <typename T>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
+    prefill_pair_kernel(const PrefillParams p, const __grid_constant__ CUtensorMap tmap_q,
+                        const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ CUtensorMap tmap_v) {
+  using L = PairLayout;
+  constexpr int D = 128;
+  constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
+  extern __shared__ __align__(1024) char smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;
+  char* sbase = smem_raw + (base - raw);
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t crank = cluster_ctarank();
+  const int cid = blockIdx.x >> 1;
+  const int nclusters = gridDim.x >> 1;
+  const int units = p.num_prefill_rows * p.hkv * p.mpairs;
+  const int G = p.group;
+
+  // Metadata errors are reported once, by the cluster that owns the unit.
+  if (threadIdx.x == 0 && crank == 0) {
+    for (int u = cid; u < units; u += nclusters) {
+      const int prow = (u / p.mpairs) / p.hkv;
+      const int row = p.rows ? __ldg(p.rows + prow) : prow;
+      if (u % (p.mpairs * p.hkv) == 0 && (row < 0 || row >= p.num_rows)) atomic_or_err(p.err, SEB_ERRBIT_META);
+      if (row >= 0 && row < p.num_rows && (u % p.mpairs) == p.mpairs - 1) {
+        const int k_len = max(__ldg(p.k_lens + row), 0);
+        if (((k_len + 15) >> 4) > p.max_blocks && (u / p.mpairs) % p.hkv == 0) atomic_or_err(p.err, SEB_ERRBIT_KLEN);
+      }
+    }
+  }
+
+  const uint32_t bar = base + L::oBar;        // this CTA's mbarrier i at bar + 8 i
+  const uint32_t lead = mapa_shared(bar, 0);  // the even CTA's
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sbase + L::oBar + 8 * kPNumBars);
+  if (threadIdx.x == 0) {
+    for (int q = 0; q < 2; ++q) {
+      mbar_init(bar + 8 * (kPBarQFull + q), 1);
+      mbar_init(bar + 8 * (kPBarQEmpty + q), 1);
+    }
+    for (int s = 0; s < kPairKStages; ++s) {
+      mbar_init(bar + 8 * (kPBarKFull + s), 1);
+      mbar_init(bar + 8 * (kPBarKEmpty + s), 1);
+    }
+    for (int s = 0; s < kPairVStages; ++s) {
+      mbar_init(bar + 8 * (kPBarVFull + s), 2);
+      mbar_init(bar + 8 * (kPBarVEmpty + s), 1);
+    }
+    for (int b = 0; b < 3; ++b) {
+      mbar_init(bar + 8 * (kPBarSFull + b), 1);
+      mbar_init(bar + 8 * (kPBarPFull + b), 16);
+      mbar_init(bar + 8 * (kPBarPFree + b), 1);
+    }
+    mbar_init(bar + 8 * kPBarDone, 2);
+    mbar_init(bar + 8 * kPBarVLand, 1);
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tc::tmem_alloc_pair(smem_u32(tmem_slot), kTmemCols);
+    tc::tmem_relinquish_pair();
+  }
+  tc::fence_before_sync();
+  cluster_sync();  // barriers initialised and TMEM allocated in both CTAs
+  tc::fence_after_sync();
+  const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(tmem_slot);
+  bool failed = false;
+  PairUnit w;
+
+  if (warp == 0 || warp == kPairVWarp) {
+    // ------------------------------------------------------------ producers
+    if (warp == 0 && lane == 0) {
+      prefetch_tensor_map(&tmap_q);
+      prefetch_tensor_map(&tmap_k);
+    }
+    if (warp == kPairVWarp && lane == 0) prefetch_tensor_map(&tmap_v);
+    int g = 0;       // tiles loaded so far (ring position)
+    int nq = 0;      // Q tiles loaded so far
+    int nland = 0;   // V tiles patched through the local barrier so far
+    for (int u = cid; u < units && !failed; u += nclusters) {
+      if (!pair_unit(p, u, w) || w.ntiles == 0) continue;
+      const int32_t* bt = p.block_table + (int64_t)w.row * p.bt_stride;
+      const int nblk = w.nblk;
+      auto fetch = [&](int win) -> int {
+        const int blk = 32 * win + lane;
+        return blk < nblk ? __ldg(bt + blk) : 0;
+      };
+      auto checked = [&](int bid) -> int {
+        if (bid < 0 || (int64_t)bid >= p.num_blocks) {
+          atomic_or_err(p.err, SEB_ERRBIT_BLOCK_ID);
+          return 0;  // read a real block instead; the row's result is flagged as invalid
+        }
+        return bid;
+      };
+      int cur = fetch(0), nxt = fetch(1), win = 0;
+      if (warp == 0) {
+        const int qb = nq & 1;
+        if (nq >= 2 && !wait_or_flag_cluster(bar + 8 * (kPBarQEmpty + qb), ((nq >> 1) - 1) & 1, failed)) break;
+        if (lane == 0) {
+          if (crank == 0) mbar_arrive_expect_tx(bar + 8 * (kPBarQFull + qb), 2 * L::kTileQ);
+#pragma unroll
+          for (int pn = 0; pn < 2; ++pn)
+            tma_load_3d_pair(base + L::oQ + qb * L::kTileQ + pn * L::kPanelQ, &tmap_q, pn * 64, w.kvh * G,
+                             w.q_start + w.pair0 + (int)crank * p.qpt, lead + 8 * (kPBarQFull + qb));
+        }
+        ++nq;
+      }
+      for (int j = 0; j < w.ntiles && !failed; ++j, ++g) {
+        while (win < (j >> 2)) {
+          cur = nxt;
+          nxt = fetch(win + 2);
+          ++win;
+        }
+        const int nb_all = min(8, nblk - 8 * j);
+        if (warp == 0) {
+          // K(j): this CTA's 4 blocks (keys [64 crank, 64 crank + 64)), both panels
+          const int s = g % kPairKStages, uu = g / kPairKStages;
+          int bid = __shfl_sync(kFullMask, cur, ((j & 3) << 3) + ((4 * (int)crank + (lane & 3)) & 7));
+          if (uu >= 1 && !wait_or_flag_cluster(bar + 8 * (kPBarKEmpty + s), (uu - 1) & 1, failed)) break;
+          const int nb = min(4, max(0, nb_all - 4 * (int)crank));
+          if (lane == 0 && crank == 0) mbar_arrive_expect_tx(bar + 8 * (kPBarKFull + s), nb_all * 2 * 2048);
+          __syncwarp();
+          if (lane < nb) {
+            bid = checked(bid);
+            const uint32_t dst = base + L::oK + s * L::kStageK + lane * 2048;
+#pragma unroll
+            for (int pn = 0; pn < 2; ++pn)
+              tma_load_3d_pair(dst + pn * L::kPanelK, &tmap_k, pn * 64, w.kvh, bid * 16,
+                               lead + 8 * (kPBarKFull + s));
+          }
+        } else {
+          // V(j): all 8 blocks, this CTA's 64 head dims. A tile whose rows past
+          // k_len (or past the loaded blocks) must read as zeros lands on a local
+          // barrier first, is patched, and then reported.
+          const int s = g % kPairVStages, uu = g / kPairVStages;
+          int bid = __shfl_sync(kFullMask, cur, ((j & 3) << 3) + (lane & 7));
+          if (uu >= 1 && !wait_or_flag_cluster(bar + 8 * (kPBarVEmpty + s), (uu - 1) & 1, failed)) break;
+          const int r0 = min(max(w.k_len - j * kBN, 0), nb_all * 16);
+          const uint32_t dst = base + L::oV + s * L::kStageV;
+          const uint32_t full_bar = bar + 8 * (kPBarVFull + s);
+          if (r0 == kBN) {
+            if (lane == 0 && crank == 0) mbar_arrive_expect_tx(full_bar, 2 * 8 * 2048);
+            __syncwarp();
+            if (lane < 8)
+              tma_load_3d_pair(dst + lane * 2048, &tmap_v, (int)crank * 64, w.kvh, checked(bid) * 16,
+                               lead + 8 * (kPBarVFull + s));
+            if (lane == 0 && crank == 1) mbar_arrive_cluster(lead + 8 * (kPBarVFull + s));
+          } else {
+            if (lane == 0) mbar_arrive_expect_tx(bar + 8 * kPBarVLand, nb_all * 2048);
+            __syncwarp();
+            if (lane < nb_all)
+              tma_load_3d(dst + lane * 2048, &tmap_v, (int)crank * 64, w.kvh, checked(bid) * 16,
+                          bar + 8 * kPBarVLand);
+            if (!wait_or_flag_cluster(bar + 8 * kPBarVLand, nland & 1, failed)) break;
+            ++nland;
+            char* vt = sbase + L::oV + s * L::kStageV;
+            for (int c = lane; c < (kBN - r0) * 8; c += 32)
+              *reinterpret_cast<uint4*>(vt + (r0 + c / 8) * 128 + (c % 8) * 16) = make_uint4(0, 0, 0, 0);
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+              if (crank == 0) mbar_arrive(full_bar);
+              else mbar_arrive_cluster(lead + 8 * (kPBarVFull + s));
+            }
+          }
+        }
+      }
+    }
+    // No copy may still be in flight when the pair exits: the even CTA's full
+    // barriers count the bytes of both CTAs.
+    if (crank == 0) {
+      bool drain_failed = false;
+      const int stages = warp == 0 ? kPairKStages : kPairVStages;
+      const int fb = warp == 0 ? kPBarKFull : kPBarVFull;
+      for (int i = max(0, g - stages); i < g; ++i)
+        wait_or_flag_cluster(bar + 8 * (fb + i % stages), (i / stages) & 1, drain_failed);
+    }
+  } else if (warp == 1 || warp == kPairSWarp) {
+    // ---------------------------------------------------------------- MMA
+    if (crank == 0) {
+      constexpr uint32_t idesc_qk = tc::idesc_f16(kBf16, false, 256, kBN);
+      constexpr uint32_t idesc_pv = tc::idesc_f16(kBf16, true, 256, D);
+      int g = 0, nq = 0;
+      for (int u = cid; u < units && !failed; u += nclusters) {
+        if (!pair_unit(p, u, w) || w.ntiles == 0) continue;
+        if (warp == kPairSWarp) {
+          // S(j) = Q K(j)^T into S buffer g % 3
+          const int qb = nq & 1;
+          if (!wait_or_flag_cluster(bar + 8 * (kPBarQFull + qb), (nq >> 1) & 1, failed)) break;
+          for (int j = 0; j < w.ntiles && !failed; ++j, ++g) {
+            const int b = g % 3, s = g % kPairKStages;
+            if (!wait_or_flag_cluster(bar + 8 * (kPBarKFull + s), (g / kPairKStages) & 1, failed)) break;
+            if (g >= 3 && !wait_or_flag_cluster(bar + 8 * (kPBarPFree + b), ((g - 3) / 3) & 1, failed)) break;
+            tc::fence_after_sync();
+            if (lane == 0) {
+#pragma unroll
+              for (int kk = 0; kk < D / 16; ++kk) {
+                const uint64_t a = tc::smem_desc_sw128(
+                    base + L::oQ + qb * L::kTileQ + (kk >> 2) * L::kPanelQ + (kk & 3) * 32, 16, 1024);
+                const uint64_t bd = tc::smem_desc_sw128(
+                    base + L::oK + s * L::kStageK + (kk >> 2) * L::kPanelK + (kk & 3) * 32, 16, 1024);
+                tc::mma_ss_pair(tmem + 128 * b, a, bd, idesc_qk, kk > 0);
+              }
+              tc::commit_pair(bar + 8 * (kPBarSFull + b), 3);
+              tc::commit_pair(bar + 8 * (kPBarKEmpty + s), 3);
+              if (j == w.ntiles - 1) tc::commit_pair(bar + 8 * (kPBarQEmpty + qb), 3);
+            }
+            __syncwarp();
+          }
+          ++nq;
+        } else {
+          // O += P(j) V(j), P read from TMEM (and its remainder for split pairs)
+          for (int j = 0; j < w.ntiles && !failed; ++j, ++g) {
+            const int b = g % 3, s = g % kPairVStages;
+            if (!wait_or_flag_cluster(bar + 8 * (kPBarVFull + s), (g / kPairVStages) & 1, failed)) break;
+            if (!wait_or_flag_cluster(bar + 8 * (kPBarPFull + b), (g / 3) & 1, failed)) break;
+            tc::fence_after_sync();
+            if (lane == 0) {
+#pragma unroll
+              for (int kk = 0; kk < kBN / 16; ++kk) {
+                const uint64_t bd =
+                    tc::smem_desc_sw128(base + L::oV + s * L::kStageV + kk * 2048, L::kStageV, 1024);
+                tc::mma_ts_pair(tmem + kPairColO, tmem + 128 * b + 8 * kk, bd, idesc_pv, j > 0 || kk > 0);
+              }
+              if (w.split) {
+#pragma unroll
+                for (int kk = 0; kk < kBN / 16; ++kk) {
+                  const uint64_t bd =
+                      tc::smem_desc_sw128(base + L::oV + s * L::kStageV + kk * 2048, L::kStageV, 1024);
+                  tc::mma_ts_pair(tmem + kPairColO, tmem + 128 * b + 64 + 8 * kk, bd, idesc_pv, true);
+                }
+              }
+              tc::commit_pair(bar + 8 * (kPBarPFree + b), 3);
+              tc::commit_pair(bar + 8 * (kPBarVEmpty + s), 3);
+            }
+            __syncwarp();
+          }
+        }
+      }
+      // Every MMA this warp issued has completed before either CTA releases TMEM.
+      if (lane == 0) tc::commit_pair(bar + 8 * kPBarDone, 3);
+      __syncwarp();
+    }
+    bool done_failed = false;
+    wait_or_flag_cluster(bar + 8 * kPBarDone, 0, done_failed);
+  } else if (warp < kPairVWarp) {
+    // ------------------------------------------------------------ softmax
+    const int q4 = warp & 3;
+    const int khalf = (warp - 2) >> 2;  // which 64 keys of a tile
+    const int m = q4 * 32 + lane;
+    const int kh0 = 64 * khalf;
+    const uint32_t taddr = tmem + ((uint32_t)(q4 * 32) << 16);
+    const float c = p.scale_log2;
+    float* xchg = reinterpret_cast<float*>(sbase + L::oX);  // [parity][half][row]
+    int g = 0;
+    for (int u = cid; u < units; u += nclusters) {
+      if (!pair_unit(p, u, w)) continue;
+      const int i0 = w.pair0 + (int)crank * p.qpt;  // this CTA's first query
+      const int qi = i0 + m / G;
+      const int gh = m % G;
+      const bool row_valid = qi <= w.i_last;
+      T* op = reinterpret_cast<T*>(p.out) + (int64_t)(w.q_start + qi) * p.o_st + (int64_t)(w.kvh * G + gh) * p.o_sh;
+      float* lp = p.lse + (int64_t)(w.q_start + qi) * p.lse_st + w.kvh * G + gh;
+      if (w.ntiles == 0) {
+        // No visible keys: the reference's loop never runs, O = 0/0, LSE = -inf.
+        if (row_valid) {
+          for (int d = kh0; d < kh0 + 64; ++d) op[d] = Elem<T>::from_float(__int_as_float(0x7fc00000));
+          if (khalf == 0) *lp = -INFINITY;
+        }
+        continue;
+      }
+      const int vis = row_valid ? (p.causal ? min(w.ceil16, w.qpos0 + qi + 1) : w.ceil16) : 0;
+      const int min_vis = p.causal ? min(w.ceil16, w.qpos0 + i0 + 1) : w.ceil16;
+      float m_ref = -INFINITY;
+      float l = 0.f;
+      for (int j = 0; j < w.ntiles; ++j, ++g) {
+        const int b = g % 3;
+        const uint32_t col_s = 128 * b;
+        wait_or_flag_cluster(bar + 8 * (kPBarSFull + b), (g / 3) & 1, failed);
+        tc::fence_after_sync();
+        const bool full = (j + 1) * kBN <= min_vis && (j + 1) * kBN <= w.k_len;
+        const float cm = full ? c : 1.f;
+        float x[2][32];
+#pragma unroll
+        for (int ch = 0; ch < 2; ++ch) tc::tmem_ld32(taddr + col_s + kh0 + 32 * ch, x[ch]);
+        tc::tmem_wait_ld();
+        if (!full) {
+#pragma unroll
+          for (int ch = 0; ch < 2; ++ch) mask_chunk(x[ch], j * kBN + kh0 + 32 * ch, vis, w.k_len, c);
+        }
+        float mx[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          mx[i] = fmaxf(fmaxf(fmaxf(x[0][i], x[0][8 + i]), fmaxf(x[0][16 + i], x[0][24 + i])),
+                        fmaxf(fmaxf(x[1][i], x[1][8 + i]), fmaxf(x[1][16 + i], x[1][24 + i])));
+        const float mh = cm * fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
+                                    fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
+        // Row max over both halves. The barrier also orders both halves' S loads
+        // before either half's P stores (P of keys 64-127 lands on S columns of
+        // keys 32-63, the remainder on those of keys 64-127).
+        float* xm = xchg + (g & 1) * 256;
+        xm[khalf * 128 + m] = mh;
+        tc::fence_before_sync();
+        named_bar_sync(1 + q4, 64);
+        tc::fence_after_sync();
+        const float mb = fmaxf(mh, xm[(1 - khalf) * 128 + m]);
+        const bool need = mb > m_ref + kLazyThreshold;
+        float factor = 1.f;
+        if (need) {
+          factor = fast_exp2(m_ref - mb);
+          l *= factor;
+          m_ref = mb;
+        }
+        const float neg_m = m_ref == -INFINITY ? 0.f : -m_ref;
+        float ls[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int ch = 0; ch < 2; ++ch) {
+          {
+            uint32_t hi[16];
+#pragma unroll
+            for (int e = 0; e < 16; ++e) {
+              const float a0 = fast_exp2(fmaf(x[ch][2 * e], cm, neg_m));
+              const float a1 = fast_exp2(fmaf(x[ch][2 * e + 1], cm, neg_m));
+              ls[e & 3] += a0 + a1;
+              hi[e] = Mma<T>::pack(a0, a1);
+              x[ch][2 * e] = a0;
+              x[ch][2 * e + 1] = a1;
+            }
+            tc::tmem_st16u(taddr + col_s + kh0 / 2 + 16 * ch, hi);
+          }
+          if (w.split) {
+            uint32_t lo[16];
+#pragma unroll
+            for (int e = 0; e < 16; ++e) {
+              const float2 f = Mma<T>::unpack(Mma<T>::pack(x[ch][2 * e], x[ch][2 * e + 1]));
+              lo[e] = Mma<T>::pack(x[ch][2 * e] - f.x, x[ch][2 * e + 1] - f.y);
+            }
+            tc::tmem_st16u(taddr + col_s + 64 + kh0 / 2 + 16 * ch, lo);
+          }
+        }
+        l += (ls[0] + ls[1]) + (ls[2] + ls[3]);
+        if (j > 0 && __any_sync(kFullMask, need)) {
+          // O must hold P V(j - 1) before it is rescaled; each half scales its 64 dims
+          const int gp = g - 1;
+          wait_or_flag_cluster(bar + 8 * (kPBarPFree + gp % 3), (gp / 3) & 1, failed);
+          tc::fence_after_sync();
+#pragma unroll 1
+          for (int cc = 0; cc < 4; ++cc) {
+            float o[16];
+            const uint32_t a = taddr + kPairColO + kh0 + 16 * cc;
+            tc::tmem_ld16(a, o);
+            tc::tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 16; ++i) o[i] *= factor;
+            tc::tmem_st16(a, o);
+          }
+        }
+        tc::tmem_wait_st();
+        tc::fence_before_sync();
+        __syncwarp();
+        if (lane == 0) {
+          if (crank == 0) mbar_arrive(bar + 8 * (kPBarPFull + b));
+          else mbar_arrive_cluster(lead + 8 * (kPBarPFull + b));
+        }
+      }
+      // ---------------------------------------------------------- epilogue
+      // Row sums of both halves: the first barrier puts every read of the last
+      // tile's maxima behind us (the sums reuse the parity-0 slots).
+      named_bar_sync(1 + q4, 64);
+      xchg[khalf * 128 + m] = l;
+      named_bar_sync(1 + q4, 64);
+      l += xchg[(1 - khalf) * 128 + m];
+      named_bar_sync(1 + q4, 64);  // the next unit's first maxima may overwrite the sums
+      // O is final once P V of the unit's last tile has completed.
+      const int gl = g - 1;
+      wait_or_flag_cluster(bar + 8 * (kPBarPFree + gl % 3), (gl / 3) & 1, failed);
+      tc::fence_after_sync();
+      if (!__any_sync(kFullMask, failed)) {
+        const float inv = 1.f / l;
+#pragma unroll
+        for (int cc = 0; cc < 2; ++cc) {
+          float o[32];
+          tc::tmem_ld32(taddr + kPairColO + kh0 + 32 * cc, o);
+          tc::tmem_wait_ld();
+          if (row_valid) {
+#pragma unroll
+            for (int v8 = 0; v8 < 4; ++v8) {
+              uint32_t wv[4];
+#pragma unroll
+              for (int e = 0; e < 4; ++e)
+                wv[e] = Mma<T>::pack(o[8 * v8 + 2 * e] * inv, o[8 * v8 + 2 * e + 1] * inv);
+              *reinterpret_cast<uint4*>(op + kh0 + 32 * cc + 8 * v8) = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+            }
+          }
+        }
+        if (row_valid && khalf == 0) *lp = m_ref * kLn2p + logf(l);
+      }
+      // The next unit's first P V overwrites O: order this warp's O loads before
+      // its next P arrival.
+      tc::fence_before_sync();
+    }
+  }
+
+  if (failed && lane == 0) atomic_or_err(p.err, SEB_ERRBIT_TIMEOUT);
+  tc::fence_before_sync();
+  cluster_sync();  // neither CTA leaves while the pair's MMAs or copies may touch it
+  if (warp == 1) {
+    tc::fence_after_sync();
+    tc::tmem_dealloc_pair(tmem, kTmemCols);
+  }
+}
+
+template <typename T>
+int launch_prefill_pair(const PrefillParams& p, const void* q, int64_t q_st, int64_t q_sh, int total_query,
+                        const void* kc, const void* vc, cudaStream_t s) {
+  constexpr int smem = PairLayout::kBytes + 1024;
+  auto kern = prefill_pair_kernel<T>;
+  static bool attr_set[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+    SEB_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    attr_set[dev] = true;
+  }
+  const int dtype = std::is_same<T, __nv_bfloat16>::value ? SEB_BF16 : SEB_F16;
+  CUtensorMap tq, tk, tv;
+  const uint64_t qdims[3] = {128, (uint64_t)p.hq, (uint64_t)total_query};
+  const uint64_t qstr[2] = {(uint64_t)q_sh * 2, (uint64_t)q_st * 2};
+  const uint32_t qbox[3] = {64, (uint32_t)p.group, (uint32_t)p.qpt};
+  int rc = tensor_map_3d(&tq, q, dtype, qdims, qstr, qbox);
+  if (rc != SEB_OK) return rc;
+  rc = kv_tensor_map(&tk, kc, dtype, p.num_blocks, p.hkv, 128);
+  if (rc != SEB_OK) return rc;
+  rc = kv_tensor_map(&tv, vc, dtype, p.num_blocks, p.hkv, 128);
+  if (rc != SEB_OK) return rc;
+  // persistent: one cluster per pair of SMs (or per unit, when there are fewer)
+  const int64_t units = (int64_t)p.num_prefill_rows * p.hkv * p.mpairs;
+  const int64_t clusters = std::min<int64_t>(units, num_sms() / 2);
+  kern<<<(unsigned)(2 * clusters), kPairThreads, smem, s>>>(p, tq, tk, tv);
+  return launch_status("prefill_pair_kernel");
+}
+
 template <typename T, int D>
 int launch_prefill(const PrefillParams& p, const void* q, int64_t q_st, int64_t q_sh, int total_query,
                    const void* kc, const void* vc, cudaStream_t s) {
@@ -630,13 +1183,14 @@ extern "C" int seb_paged_prefill(const void* q, int64_t q_stride_token, int64_t 
   const int64_t grid = (int64_t)num_prefill_rows * num_kv_heads * p.mpairs * 2;
   SEB_CHECK_ARG(grid < (1ll << 31), "seb_paged_prefill: grid too large");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // head_dim 128: the CTA-pair kernel; head_dim 64: one CTA per pair of Q tiles
   if (dtype == SEB_BF16) {
-    return head_dim == 128 ? launch_prefill<__nv_bfloat16, 128>(p, q, q_stride_token, q_stride_head, total_query,
+    return head_dim == 128 ? launch_prefill_pair<__nv_bfloat16>(p, q, q_stride_token, q_stride_head, total_query,
                                                                 k_cache, v_cache, s)
                            : launch_prefill<__nv_bfloat16, 64>(p, q, q_stride_token, q_stride_head, total_query,
                                                                k_cache, v_cache, s);
   }
   return head_dim == 128
-             ? launch_prefill<__half, 128>(p, q, q_stride_token, q_stride_head, total_query, k_cache, v_cache, s)
+             ? launch_prefill_pair<__half>(p, q, q_stride_token, q_stride_head, total_query, k_cache, v_cache, s)
              : launch_prefill<__half, 64>(p, q, q_stride_token, q_stride_head, total_query, k_cache, v_cache, s);
 }
