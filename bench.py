@@ -76,10 +76,10 @@ def peaks():
     return FALLBACK_HBM_GBS, "fallback"
 
 
-def profiled_traffic():
-    """dram bytes per launch of the decode kernel from the committed ncu summary
-    (a line 'traffic_bytes_per_launch: N'), or None."""
-    p = REPO / "profiles" / "paged_decode_config2.md"
+def profiled_traffic(summary: str = "paged_decode_config2.md"):
+    """dram bytes per launch of a kernel from its committed ncu summary (a line
+    'traffic_bytes_per_launch: N'), or None."""
+    p = REPO / "profiles" / summary
     if not p.exists():
         return None
     m = re.search(r"traffic_bytes_per_launch:\s*([0-9.eE+]+)", p.read_text())
@@ -508,7 +508,8 @@ def run_prefill_workload(args, device):
                           "cow_copy_blocks": round(cow_bytes / (cow_ms * 1e-3) / 1e9, 1)},
         "roofline": {"bound": "tensor", "achieved": round(tflops, 1), "peak": pk.get("bf16_tflops"),
                      "unit": "TFLOP/s", "frac": round(tflops / pk.get("bf16_tflops", 1590.0), 4),
-                     "peak_source": "measured burst (MEASURED_PEAKS.json bf16_tflops)", "traffic": None},
+                     "peak_source": "measured burst (MEASURED_PEAKS.json bf16_tflops)",
+                     "traffic": profiled_traffic("prefill_pair_config3.md"), "traffic_unit": "dram bytes per launch"},
     }
 
 
