@@ -110,3 +110,32 @@ def test_ctypes_signatures_match_header_arity():
         assert m, name
         params = [p for p in m.group(1).split(",") if p.strip() and p.strip() != "void"]
         assert len(params) == len(args), (name, len(params), len(args))
+
+
+def _ar_args(world=2, hidden=512, dtype=None, ptr=1 << 20, weight=1 << 21, rank=0, all_ranks=0):
+    """Arguments of seb_allreduce_add_rmsnorm with host pointer arrays of fake,
+    16-byte aligned device addresses (validation never dereferences them)."""
+    arr = lambda: (ctypes.c_void_p * max(world, 1))(*[ptr + 4096 * q for q in range(max(world, 1))])
+    return (arr(), arr(), arr(), arr(), weight, 256, hidden, ctypes.c_float(1e-5),
+            _lib.SEB_BF16 if dtype is None else dtype, rank, world, all_ranks, 0, None, None)
+
+
+def test_allreduce_add_rmsnorm_validation(lib):
+    assert lib.seb_allreduce_add_rmsnorm(*_ar_args(world=_lib.SEB_MAX_PEERS + 1)) == _lib.SEB_EINVAL
+    assert b"world" in lib.seb_last_error()
+    assert lib.seb_allreduce_add_rmsnorm(*_ar_args(world=0)) == _lib.SEB_EINVAL
+    assert lib.seb_allreduce_add_rmsnorm(*_ar_args(hidden=500)) == _lib.SEB_EINVAL  # not a multiple of 8
+    assert b"hidden" in lib.seb_last_error()
+    assert lib.seb_allreduce_add_rmsnorm(*_ar_args(dtype=_lib.SEB_F32)) == _lib.SEB_EINVAL
+    assert lib.seb_allreduce_add_rmsnorm(*_ar_args(rank=2)) == _lib.SEB_EINVAL  # rank outside the world
+    assert lib.seb_allreduce_add_rmsnorm(*_ar_args(rank=1, all_ranks=1)) == _lib.SEB_EINVAL
+    assert lib.seb_allreduce_add_rmsnorm(*_ar_args(ptr=(1 << 20) + 8)) == _lib.SEB_EINVAL  # misaligned buffers
+    assert b"aligned" in lib.seb_last_error()
+    assert lib.seb_allreduce_add_rmsnorm(*_ar_args(weight=0)) == _lib.SEB_EINVAL
+    assert b"NULL" in lib.seb_last_error()
+
+
+def test_peer_memory_calls_reject_null(lib):
+    assert lib.seb_peer_alloc(0, None) == _lib.SEB_EINVAL
+    assert lib.seb_peer_export(None, None) == _lib.SEB_EINVAL
+    assert lib.seb_peer_import(None, None) == _lib.SEB_EINVAL
