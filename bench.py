@@ -65,6 +65,9 @@ def parse_args():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer e2e leg (short profiling runs)")
     ap.add_argument("--e2e-budget", type=int, default=8192, help="max_num_batched_tokens of the config-4 engine")
+    ap.add_argument("--prefix-len", type=int, default=2040,
+                    help="prefill: tokens of the shared prefix (config 3: 2040; 0: fresh prompts)")
+    ap.add_argument("--chunk-len", type=int, default=512, help="prefill: tokens each row prefills (config 3: 512)")
     return ap.parse_args()
 
 
@@ -455,7 +458,8 @@ def run_prefill_workload(args, device):
     from serving_engine_b200 import ops, paged_flash_attention, workloads
     from serving_engine_b200.paged_attention import metadata_from_lists
 
-    b = workloads.config3(seed=args.seed, prefix_len=2040, fill=str(device))
+    b = workloads.prefix_prefill_batch(16, args.prefix_len, args.chunk_len, 32, 8, 128, torch.bfloat16, args.seed,
+                                       fill=str(device))
     md = metadata_from_lists(b.q_lens, b.k_lens, b.q_starts, b.q_pos_offsets, b.block_tables, device)
     q = b.q.to(device)
     nk, nv = b.extra["new_k"].to(device), b.extra["new_v"].to(device)
@@ -500,12 +504,15 @@ def run_prefill_workload(args, device):
         "metric": "chunked-prefill attention TFLOP/s (config 3)", "value": round(tflops, 1), "unit": "TFLOP/s",
         "n_gpus": 1, "steps": n, "warmup": args.warmup, "ms_per_step": round(att_ms + cow_ms + app_ms, 4),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": "config 3: 16 rows, shared 2040-token prefix, 512-token causal chunks, 32q/8kv, D=128",
+        "config": {"workload": (f"config 3: 16 rows, shared {args.prefix_len}-token prefix, {args.chunk_len}-token causal "
+                                "chunks, 32q/8kv, D=128") if (args.prefix_len, args.chunk_len) == (2040, 512) else
+                   (f"config-3 variant: 16 rows, shared {args.prefix_len}-token prefix, {args.chunk_len}-token causal "
+                    "chunks, 32q/8kv, D=128"),
                    "attention_gflop": round(flops / 1e9, 1)},
         "breakdown_ms": {"cow_copy_blocks": round(cow_ms, 4), "kv_append": round(app_ms, 4),
                          "prefill_attention": round(att_ms, 4)},
         "bandwidth_gbs": {"kv_append": round(app_bytes / (app_ms * 1e-3) / 1e9, 1),
-                          "cow_copy_blocks": round(cow_bytes / (cow_ms * 1e-3) / 1e9, 1)},
+                          "cow_copy_blocks": round(cow_bytes / (cow_ms * 1e-3) / 1e9, 1) if cow_bytes else None},
         "roofline": {"bound": "tensor", "achieved": round(tflops, 1), "peak": pk.get("bf16_tflops"),
                      "unit": "TFLOP/s", "frac": round(tflops / pk.get("bf16_tflops", 1590.0), 4),
                      "peak_source": "measured burst (MEASURED_PEAKS.json bf16_tflops)",
