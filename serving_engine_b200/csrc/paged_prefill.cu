@@ -836,6 +836,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
             const int b = g % 3, s = g % kPairKStages;
             if (!wait_or_flag_cluster(bar + 8 * (kPBarKFull + s), (g / kPairKStages) & 1, failed)) break;
             if (g >= 3 && !wait_or_flag_cluster(bar + 8 * (kPBarPFree + b), ((g - 3) / 3) & 1, failed)) break;
+            // A unit's first S waits for the previous unit's last P V, so that P V
+            // (whose completion the previous unit's epilogue waits on) is not
+            // queued behind it on the tensor pipe.
+            if (j == 0 && g >= 1 &&
+                !wait_or_flag_cluster(bar + 8 * (kPBarPFree + (g - 1) % 3), ((g - 1) / 3) & 1, failed))
+              break;
             tc::fence_after_sync();
             if (lane == 0) {
 #pragma unroll
