@@ -209,15 +209,18 @@ def decode_workspace_bytes(num_items: int, num_q_heads: int, num_kv_heads: int, 
 
 
 @_nvtx
-def decode_blocks_per_split(num_items: int, num_kv_heads: int, blocks_per_row: int, device=None) -> int:
+def decode_blocks_per_split(num_items: int, num_kv_heads: int, blocks_per_row: int, device=None,
+                            num_sms: int | None = None) -> int:
     """Split length for seb_paged_decode when every row's length is known (here
     all rows hold `blocks_per_row` blocks): the longest split, at most 32
     blocks, that still gives the kernel about 1.5 waves of warps (12 resident
     per SM). Long splits cut the merge work, and a wave count near 1 leaves SMs
     idle at the tail. The library's own default assumes rows fill half the
-    block table."""
-    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
-    slots = torch.cuda.get_device_properties(dev).multi_processor_count * 12
+    block table. `num_sms` defaults to the device's SM count."""
+    if num_sms is None:
+        dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+        num_sms = torch.cuda.get_device_properties(dev).multi_processor_count
+    slots = num_sms * 12
     for bps in range(32, 7, -1):
         if num_items * num_kv_heads * -(-blocks_per_row // bps) >= 1.5 * slots:
             return bps
