@@ -10,8 +10,9 @@ paged_flash_attention call over the whole batch (one layer of one decode step).
 
 With N GPUs (torchrun, one process per GPU) the (sequence, kv head) units are
 sharded by kv head: each rank owns 8/N kv heads (32/N q heads) of a global
-batch of 64*N sequences, so per-GPU work stays at the config-2 size (weak
-scaling) and no data crosses GPUs. ``value`` is the aggregate KV bytes read
+batch of 64*N sequences whose k_len list is the 1-GPU list repeated N times, so
+every rank reads exactly the config-2 bytes (weak scaling) and no data crosses
+GPUs. ``value`` is the aggregate KV bytes read
 per second over all ranks, timed as the max over ranks.
 
 ``e2e`` is the same metric through the public API with host buffers: each step
@@ -30,7 +31,6 @@ import argparse
 import json
 import math
 import os
-import re
 import statistics
 import subprocess
 import sys
@@ -79,18 +79,23 @@ def peaks():
     return FALLBACK_HBM_GBS, "fallback"
 
 
-def profiled_traffic(summary: str = "paged_decode_config2.md"):
-    """dram bytes per launch of a kernel from its committed ncu summary (a line
-    'traffic_bytes_per_launch: N'), or None."""
-    p = REPO / "profiles" / summary
+def profiled_traffic(kernel: str = "decode_mma_kernel"):
+    """DRAM bytes per launch of `kernel` (read + write) from one ncu capture of the
+    same workload, kept in profiles/traffic.json; None when absent."""
+    p = REPO / "profiles" / "traffic.json"
     if not p.exists():
         return None
-    m = re.search(r"traffic_bytes_per_launch:\s*([0-9.eE+]+)", p.read_text())
-    return float(m.group(1)) if m else None
+    entry = json.loads(p.read_text()).get(kernel)
+    return float(entry["dram_bytes_per_launch"]) if entry else None
 
 
 class ClockSampler:
-    """nvidia-smi clock/throttle samples every 100 ms while the timed region runs."""
+    """nvidia-smi clock/throttle samples every 100 ms, read by a background thread.
+
+    A timed region of a few milliseconds is shorter than one sampling interval,
+    so ``busy_until_sampled`` keeps the GPU running the same step (untimed) until
+    the sampler has taken some samples; the samples then cover that pre-warm
+    load and the timed region that follows it with no idle gap."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -99,21 +104,51 @@ class ClockSampler:
     def __init__(self, gpu_index: int):
         self.idx = gpu_index
         self.proc = None
+        self.lines: list[str] = []
+        self.thread = None
 
     def start(self):
+        import threading
+
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.idx), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
                  "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except OSError:
             self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            if line.strip():
+                self.lines.append(line.strip())
+
+    def busy_until_sampled(self, busy, samples: int = 3, timeout_s: float = 10.0) -> int:
+        """Call busy() (untimed GPU work that ends with a synchronize) until
+        `samples` samples were taken after the first call; returns the calls made."""
+        if self.proc is None:
+            return 0
+        t_end = time.time() + timeout_s
+        busy()
+        n0, calls = len(self.lines), 1
+        while len(self.lines) < n0 + samples and time.time() < t_end:
+            busy()
+            calls += 1
+        return calls
 
     def stop(self) -> dict:
         if self.proc is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"], "samples": 0}
         self.proc.terminate()
-        out, _ = self.proc.communicate(timeout=10)
-        rows = [[c.strip() for c in line.split(",")] for line in out.strip().splitlines() if line.strip()]
+        try:
+            self.proc.wait(timeout=10)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        if self.thread is not None:
+            self.thread.join(timeout=10)
+        rows = [[c.strip() for c in line.split(",")] for line in self.lines]
         sm = [float(r[1]) for r in rows if len(r) >= 9 and r[1].replace(".", "").isdigit()]
         smax = [float(r[2]) for r in rows if len(r) >= 9 and r[2].replace(".", "").isdigit()]
         reasons = set()
@@ -132,10 +167,16 @@ class ClockSampler:
 def shard_spec(batch: int, world: int, rank: int, seed: int, hq: int = 32, hkv: int = 8) -> dict:
     """Rank `rank`'s share of the kv-head-sharded decode workload: a global batch
     of batch*world sequences, of which this rank holds hkv/world kv heads (and
-    hq/world q heads) of every sequence, so per-rank work equals the 1-GPU work."""
+    hq/world q heads) of every sequence. The k_len list is the 1-GPU draw of
+    `seed` repeated world times, so every rank reads exactly the 1-GPU bytes at
+    every world size; only the values (q, pool, tables) differ between ranks."""
     if hkv % world or hq % world:
         raise ValueError(f"{world} ranks must divide the {hkv} kv heads and {hq} q heads")
-    return {"batch": batch * world, "hq": hq // world, "hkv": hkv // world, "seed": seed * 1000 + rank}
+    from serving_engine_b200.workloads import decode_k_lens
+
+    k_lens = decode_k_lens(batch, 1024, 8192, seed) * world
+    return {"batch": batch * world, "hq": hq // world, "hkv": hkv // world, "seed": seed * 1000 + rank,
+            "k_lens": k_lens}
 
 
 def max_over_ranks(dist, value: float, device) -> float:
@@ -147,12 +188,22 @@ def max_over_ranks(dist, value: float, device) -> float:
     return float(t.item())
 
 
+def gather_over_ranks(dist, value: float, device) -> list[float]:
+    """Every rank's value (rank order)."""
+    if dist is None:
+        return [value]
+    t = torch.tensor([value], dtype=torch.float64, device=device)
+    out = [torch.empty_like(t) for _ in range(dist.get_world_size())]
+    dist.all_gather(out, t)
+    return [float(x.item()) for x in out]
+
+
 def shard_batch(args, rank: int, world: int, device):
     from serving_engine_b200 import workloads
 
     sp = shard_spec(args.batch, world, rank, args.seed)
     return workloads.decode_batch(sp["batch"], 1024, 8192, sp["hq"], sp["hkv"], 128, torch.bfloat16,
-                                  seed=sp["seed"], fill=str(device))
+                                  seed=sp["seed"], fill=str(device), k_lens=sp["k_lens"])
 
 
 def run_ours(args, rank, world, device, dist):
@@ -169,17 +220,25 @@ def run_ours(args, rank, world, device, dist):
     def step():
         return paged_flash_attention(q, b.k_cache, b.v_cache, md, hq, hkv, b.scale)
 
-    for _ in range(max(args.warmup, 3)):
-        step()
+    # One untimed call checks the device error word; the clock sampler then starts
+    # and the warm-up steps run straight into the timed region (no idle gap in
+    # which the GPU could leave its working clocks).
+    step()
     torch.cuda.synchronize(device)
     ops.check_device_errors(device)
-
     sampler = ClockSampler(device.index if device.index is not None else 0)
+    sampler.start()
+
+    def prewarm():
+        for _ in range(50):
+            step()
+        torch.cuda.synchronize(device)
+
+    prewarm_calls = sampler.busy_until_sampled(prewarm)
     if dist is not None:
         dist.barrier()
-    torch.cuda.synchronize(device)
-    sampler.start()
-    time.sleep(0.3)  # let nvidia-smi start sampling before the timed region
+    for _ in range(max(args.warmup, 3)):
+        step()
     launches0 = ops.LAUNCHES[0]
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     ev0.record(stream)
@@ -190,13 +249,13 @@ def run_ours(args, rank, world, device, dist):
     launches = ops.LAUNCHES[0] - launches0
     clocks = sampler.stop()
     ms_total = ev0.elapsed_time(ev1)
-    ms_total_max = max_over_ranks(dist, ms_total, device)
+    per_rank_ms = gather_over_ranks(dist, ms_total / args.steps, device)
+    ms_per_step = max(per_rank_ms)
     if dist is not None:
         dist.barrier()
-    ms_per_step = ms_total_max / args.steps
     agg_bytes = kv_bytes_rank * world
     value = agg_bytes / (ms_per_step * 1e-3) / 1e9
-    per_rank_gbs = kv_bytes_rank / (ms_total / args.steps * 1e-3) / 1e9
+    per_rank_gbs = kv_bytes_rank / (ms_per_step * 1e-3) / 1e9
     ops.check_device_errors(device)
 
     # ---- e2e through the public API with host buffers
@@ -224,12 +283,15 @@ def run_ours(args, rank, world, device, dist):
             "kv_bytes_per_step_per_gpu": kv_bytes_rank,
             "l2": "inputs larger than L2 (KV ~1.2 GB per step per GPU vs 126 MB L2); no flush",
         },
+        "per_rank_ms_per_step": {"min": round(min(per_rank_ms), 5), "max": round(max(per_rank_ms), 5),
+                                 "ranks": len(per_rank_ms)},
         "gpu_launches": launches,
-        "clocks": clocks,
+        "clocks": dict(clocks, sampled_over=f"{50 * prewarm_calls} untimed pre-warm steps (the same call) run "
+                                            "straight into the warm-up and timed steps"),
         "e2e": e2e,
     }
     hbm, src = peaks()
-    traffic = profiled_traffic()
+    traffic = profiled_traffic("decode_mma_kernel")
     result["roofline"] = {
         "bound": "hbm",
         "achieved": round(per_rank_gbs, 2),
@@ -240,6 +302,7 @@ def run_ours(args, rank, world, device, dist):
         "frac_of_nominal_8000": round(per_rank_gbs / 8000.0, 4),
         "kernel": "decode_mma_kernel (split-K with in-kernel merge; one paged_flash_attention call)",
         "traffic": traffic,
+        "traffic_source": "profiles/traffic.json (one ncu capture of this per-GPU workload)",
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         result["cpu_baseline"] = cpu_baseline(b, budget_s=12.0)
@@ -290,7 +353,7 @@ def run_e2e(args, b, device, dist, world):
         if i >= 1:
             done[k ^ 1].synchronize()  # step i-1's result is on the host
 
-    n = max(10, min(args.steps // 10, 200))
+    n = max(200, args.steps)
     for i in range(3):
         step(i)
     torch.cuda.synchronize(device)
@@ -516,7 +579,7 @@ def run_prefill_workload(args, device):
         "roofline": {"bound": "tensor", "achieved": round(tflops, 1), "peak": pk.get("bf16_tflops"),
                      "unit": "TFLOP/s", "frac": round(tflops / pk.get("bf16_tflops", 1590.0), 4),
                      "peak_source": "measured burst (MEASURED_PEAKS.json bf16_tflops)",
-                     "traffic": profiled_traffic("prefill_pair_config3.md"), "traffic_unit": "dram bytes per launch"},
+                     "traffic": profiled_traffic("prefill_pair_kernel"), "traffic_unit": "dram bytes per launch"},
     }
 
 

@@ -93,9 +93,12 @@ SEB_API int seb_kv_append(const void* k_new, int64_t k_stride_token, int64_t k_s
  * (block_manager.py:129-132) shares whole tables and never copies.
  * `layer_stride_bytes` is the distance between layer l and l+1 in bytes (the
  * full pool passes 2*num_blocks*block_bytes; a per-layer call passes any value
- * with num_layers = 1). dst ids must be distinct and must not appear among src
- * ids (validated by the caller; overlapping pairs race). Ids outside
- * [0, num_blocks) set SEB_ERRBIT_BLOCK_ID and are skipped.
+ * with num_layers = 1). All pairs are copied at once by one grid, so the
+ * result is defined only when the dst ids are distinct and no dst id appears
+ * among the src ids of the same call; otherwise it depends on thread timing.
+ * The library does not check this (the ids are device data); the Python
+ * wrapper checks host lists. Ids outside [0, num_blocks) set
+ * SEB_ERRBIT_BLOCK_ID and are skipped.
  */
 SEB_API int seb_copy_blocks(void* kv_cache, int64_t num_layers, int64_t layer_stride_bytes,
                     int64_t num_blocks, int64_t block_bytes, const int64_t* src,
@@ -165,6 +168,40 @@ SEB_API int seb_paged_prefill(const void* q, int64_t q_stride_token, int64_t q_s
                               void* stream);
 
 /*
+ * Paged attention over a whole mixed batch given only the reference's own step
+ * metadata (the dict of build_paged_batch_metadata,
+ * serving_engine/paged_attention_kernel.py:163-200, as the engine's
+ * ModelRunner.forward builds it at model_runner.py:184 and hands it to the
+ * launcher paged_flash_attention, paged_attention_kernel.py:125-160): per-row
+ * q_lens, k_lens, q_starts, q_pos_offsets and the zero-padded block table, all
+ * device arrays. Semantics as stated above for seb_paged_decode.
+ *
+ * The host needs to know only num_rows and total_query. When total_query >
+ * num_rows and the shape has a tcgen05 prefill kernel (bf16/fp16, head_dim 64
+ * or 128, group 1/2/4/8/16, q and out 16-byte aligned with strides that are
+ * multiples of 8), a one-CTA routing kernel splits the rows on the device:
+ * q_len == 1 rows become split-K decode items and q_len > 1 rows become tcgen05
+ * prefill work units, and both kernels read their counts from the device.
+ * Otherwise every token runs through the split-K kernel. Three launches at
+ * most; no host synchronisation.
+ * workspace: at least seb_paged_attention_workspace_size(...) bytes, 256-byte
+ *   aligned, not shared by calls that overlap on the GPU; nothing in it needs
+ *   to start at zero.
+ */
+SEB_API int64_t seb_paged_attention_workspace_size(int32_t num_rows, int32_t total_query, int32_t num_q_heads,
+                                                   int32_t num_kv_heads, int32_t head_dim, int64_t max_blocks);
+
+SEB_API int seb_paged_attention(const void* q, int64_t q_stride_token, int64_t q_stride_head, const void* k_cache,
+                                const void* v_cache, int64_t num_blocks, const int32_t* block_table,
+                                int64_t block_table_stride, int64_t max_blocks, const int32_t* q_lens,
+                                const int32_t* k_lens, const int32_t* q_starts, const int32_t* q_pos_offsets,
+                                int32_t num_rows, int32_t total_query, int32_t num_q_heads, int32_t num_kv_heads,
+                                int32_t head_dim, int32_t dtype, float scale, int32_t is_causal, void* out,
+                                int64_t out_stride_token, int64_t out_stride_head, float* lse,
+                                int64_t lse_stride_token, void* workspace, int64_t workspace_bytes, int32_t* err,
+                                void* stream);
+
+/*
  * Allocation-free variant of seb_paged_decode. This entry point has no
  * counterpart in the reference: it exists for callers that cannot hand the
  * library a workspace, such as a host runtime whose allocator already owns all
@@ -176,14 +213,20 @@ SEB_API int seb_paged_prefill(const void* q, int64_t q_stride_token, int64_t q_s
  * SEB_NOALLOC_SCRATCH_BYTES (32 MiB), which every GPU that loads the library
  * holds until the process exits. A call whose scratch need
  * (seb_paged_decode_workspace_size) exceeds it returns SEB_EWORKSPACE with a
- * message and launches nothing; callers can raise blocks_per_split or split the
- * batch. The call itself never calls cudaMalloc or cudaFree.
+ * message and launches nothing. Raising blocks_per_split shrinks the need only
+ * up to its cap of 32 blocks per split: the smallest need of a batch is
+ *   num_items * num_q_heads * ceil(max_blocks / 32) * (head_dim + 2) * 4 bytes
+ *   + num_items * num_kv_heads * 4 bytes (rounded up to 16),
+ * and a batch above 32 MiB even there must be split into smaller calls. The
+ * call itself never calls cudaMalloc or cudaFree.
  *
- * The first call on each device looks up the array's device address
+ * The first call on each device that needs scratch (num_items > 0 and some row
+ * longer than one split) looks up the array's device address
  * (cudaGetSymbolAddress, with that device current) and caches it; make that
- * first call outside any stream capture. All calls share the one array and
- * nothing in it needs to start at zero, but calls that overlap on the GPU (for
- * example on two streams at once) race on it and must be serialised.
+ * first call outside any stream capture. Calls that need no scratch never look
+ * it up. All calls share the one array and nothing in it needs to start at
+ * zero, but calls that overlap on the GPU (for example on two streams at once)
+ * race on it and must be serialised.
  */
 #define SEB_NOALLOC_SCRATCH_BYTES (32ll << 20)
 

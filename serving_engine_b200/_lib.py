@@ -69,6 +69,20 @@ SIGNATURES = {
          c_void_p, c_int64,                     # lse, stride
          c_void_p, c_void_p],                   # err, stream
     ),
+    "seb_paged_attention_workspace_size": (c_int64, [c_int32, c_int32, c_int32, c_int32, c_int32, c_int64]),
+    "seb_paged_attention": (
+        c_int32,
+        [c_void_p, c_int64, c_int64,            # q, strides
+         c_void_p, c_void_p, c_int64,           # k_cache, v_cache, num_blocks
+         c_void_p, c_int64, c_int64,            # block_table, stride, max_blocks
+         c_void_p, c_void_p, c_void_p, c_void_p,  # q_lens, k_lens, q_starts, q_pos_offsets
+         c_int32, c_int32,                      # num_rows, total_query
+         c_int32, c_int32, c_int32, c_int32,    # hq, hkv, head_dim, dtype
+         c_float, c_int32,                      # scale, is_causal
+         c_void_p, c_int64, c_int64,            # out, strides
+         c_void_p, c_int64,                     # lse, stride
+         c_void_p, c_int64, c_void_p, c_void_p],  # workspace, bytes, err, stream
+    ),
     # seb_paged_decode without the workspace pair (built-in scratch)
     "seb_paged_decode_noalloc": (
         c_int32,

@@ -57,6 +57,7 @@ struct DecodeParams {
   const int32_t* item_query;
   const int32_t* item_row;
   int32_t num_items;
+  const int32_t* num_items_dev;  // when set: only items < *num_items_dev (<= num_items) run
   int32_t hq, hkv, group;
   float scale_log2;
   int32_t causal;
@@ -303,7 +304,7 @@ __global__ void __launch_bounds__(WARPS * 32)
   const int64_t tmp = w / p.max_splits;
   const int kvh = (int)(tmp % p.hkv);
   const int64_t item = tmp / p.hkv;
-  if (item >= p.num_items) return;
+  if (item >= p.num_items || (p.num_items_dev && item >= __ldg(p.num_items_dev))) return;
 
   const ItemInfo it = item_info(p, (int)item);
   if (split == 0 && kvh == 0) report_item(p, it, lane);
@@ -603,7 +604,7 @@ __global__ void __launch_bounds__(WARPS * 32) decode_simt_kernel(const DecodePar
   const int64_t tmp = w / p.max_splits;
   const int kvh = (int)(tmp % p.hkv);
   const int64_t item = tmp / p.hkv;
-  if (item >= p.num_items) return;
+  if (item >= p.num_items || (p.num_items_dev && item >= __ldg(p.num_items_dev))) return;
   const ItemInfo it = item_info(p, (int)item);
   if (split == 0 && kvh == 0) report_item(p, it, lane);
   if (!it.ok) return;
@@ -743,17 +744,12 @@ int launch_mma(const DecodeParams& p, int64_t n_warps, cudaStream_t s) {
   constexpr int stages = mma_stages<D>();
   constexpr int smem = 1024 /* alignment slack */ + kBarRegion + kMmaWarps * stages * TmaTile<D>::kStage;
   static_assert(kMmaWarps * stages * 8 <= kBarRegion, "mbarrier region too small");
-  auto kern = decode_mma_kernel<T, D, NTH, stages, kMmaWarps>;
-  static bool attr_set[64] = {false};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-    SEB_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    attr_set[dev] = true;
-  }
+  constexpr auto kern = decode_mma_kernel<T, D, NTH, stages, kMmaWarps>;
+  int rc = set_smem_limit_once<kern>(smem);
+  if (rc != SEB_OK) return rc;
   CUtensorMap tk, tv;
   const int dtype = std::is_same<T, __nv_bfloat16>::value ? SEB_BF16 : SEB_F16;
-  int rc = kv_tensor_map(&tk, p.k_cache, dtype, p.num_blocks, p.hkv, D);
+  rc = kv_tensor_map(&tk, p.k_cache, dtype, p.num_blocks, p.hkv, D);
   if (rc != SEB_OK) return rc;
   rc = kv_tensor_map(&tv, p.v_cache, dtype, p.num_blocks, p.hkv, D);
   if (rc != SEB_OK) return rc;
@@ -819,20 +815,17 @@ extern "C" int64_t seb_paged_decode_workspace_size(int32_t num_items, int32_t nu
          seb::counter_bytes(num_items, num_kv_heads);
 }
 
-extern "C" int seb_paged_decode(const void* q, int64_t q_stride_token, int64_t q_stride_head,
-                                const void* k_cache, const void* v_cache, int64_t num_blocks,
-                                const int32_t* block_table, int64_t block_table_stride,
-                                int64_t max_blocks, const int32_t* q_starts, const int32_t* k_lens,
-                                const int32_t* q_pos_offsets, int32_t num_rows, int32_t total_query,
-                                const int32_t* item_query, const int32_t* item_row,
-                                int32_t num_items, int32_t num_q_heads, int32_t num_kv_heads,
-                                int32_t head_dim, int32_t dtype, float scale, int32_t is_causal,
-                                int32_t blocks_per_split, void* out, int64_t out_stride_token,
-                                int64_t out_stride_head, float* lse, int64_t lse_stride_token,
-                                void* workspace, int64_t workspace_bytes, int32_t* err,
-                                void* stream) {
-  using namespace seb;
-  clear_error();
+namespace seb {
+
+int paged_decode_impl(const void* q, int64_t q_stride_token, int64_t q_stride_head, const void* k_cache,
+                      const void* v_cache, int64_t num_blocks, const int32_t* block_table, int64_t block_table_stride,
+                      int64_t max_blocks, const int32_t* q_starts, const int32_t* k_lens, const int32_t* q_pos_offsets,
+                      int32_t num_rows, int32_t total_query, const int32_t* item_query, const int32_t* item_row,
+                      int32_t num_items, const int32_t* num_items_dev, int32_t num_q_heads, int32_t num_kv_heads,
+                      int32_t head_dim, int32_t dtype, float scale, int32_t is_causal, int32_t blocks_per_split,
+                      void* out, int64_t out_stride_token, int64_t out_stride_head, float* lse,
+                      int64_t lse_stride_token, void* workspace, int64_t workspace_bytes, int32_t* err,
+                      void* stream) {
   const int es = elem_size(dtype);
   SEB_CHECK_ARG(es > 0, "seb_paged_decode: unknown dtype %d", dtype);
   SEB_CHECK_ARG(num_items >= 0 && num_rows >= 0 && total_query >= 0, "seb_paged_decode: negative count");
@@ -873,6 +866,7 @@ extern "C" int seb_paged_decode(const void* q, int64_t q_stride_token, int64_t q
   p.item_query = item_query;
   p.item_row = item_row;
   p.num_items = num_items;
+  p.num_items_dev = num_items_dev;
   p.hq = num_q_heads;
   p.hkv = num_kv_heads;
   p.group = group;
@@ -912,6 +906,28 @@ extern "C" int seb_paged_decode(const void* q, int64_t q_stride_token, int64_t q
     case SEB_F16: return launch_dim<__half>(p, head_dim, n_warps, tc, s);
     default: return launch_dim<float>(p, head_dim, n_warps, false, s);
   }
+}
+
+}  // namespace seb
+
+extern "C" int seb_paged_decode(const void* q, int64_t q_stride_token, int64_t q_stride_head,
+                                const void* k_cache, const void* v_cache, int64_t num_blocks,
+                                const int32_t* block_table, int64_t block_table_stride,
+                                int64_t max_blocks, const int32_t* q_starts, const int32_t* k_lens,
+                                const int32_t* q_pos_offsets, int32_t num_rows, int32_t total_query,
+                                const int32_t* item_query, const int32_t* item_row,
+                                int32_t num_items, int32_t num_q_heads, int32_t num_kv_heads,
+                                int32_t head_dim, int32_t dtype, float scale, int32_t is_causal,
+                                int32_t blocks_per_split, void* out, int64_t out_stride_token,
+                                int64_t out_stride_head, float* lse, int64_t lse_stride_token,
+                                void* workspace, int64_t workspace_bytes, int32_t* err,
+                                void* stream) {
+  seb::clear_error();
+  return seb::paged_decode_impl(q, q_stride_token, q_stride_head, k_cache, v_cache, num_blocks, block_table,
+                                block_table_stride, max_blocks, q_starts, k_lens, q_pos_offsets, num_rows,
+                                total_query, item_query, item_row, num_items, nullptr, num_q_heads, num_kv_heads,
+                                head_dim, dtype, scale, is_causal, blocks_per_split, out, out_stride_token,
+                                out_stride_head, lse, lse_stride_token, workspace, workspace_bytes, err, stream);
 }
 
 // ---------------------------------------------------------------------------
@@ -974,17 +990,27 @@ extern "C" int seb_paged_decode_noalloc(const void* q, int64_t q_stride_token, i
   const int64_t need = seb_paged_decode_workspace_size(num_items, num_q_heads, num_kv_heads, head_dim, max_blocks,
                                                        blocks_per_split);
   if (need > (int64_t)SEB_NOALLOC_SCRATCH_BYTES) {
+    // The smallest need any blocks_per_split reaches is the one at the cap of 32
+    // blocks per split; past it only a smaller batch helps.
+    const int64_t floor_need = seb_paged_decode_workspace_size(num_items, num_q_heads, num_kv_heads, head_dim,
+                                                               max_blocks, kMaxBps);
     set_error("seb_paged_decode_noalloc: this call needs %lld bytes of split-K scratch but the built-in scratch "
-              "holds %lld bytes; use fewer items, more blocks_per_split, or seb_paged_decode with a workspace",
-              (long long)need, (long long)SEB_NOALLOC_SCRATCH_BYTES);
+              "holds %lld bytes; blocks_per_split is capped at %d, where this batch still needs %lld bytes: "
+              "split the batch, or call seb_paged_decode with a workspace",
+              (long long)need, (long long)SEB_NOALLOC_SCRATCH_BYTES, kMaxBps, (long long)floor_need);
     return SEB_EWORKSPACE;
   }
+  // A call that needs no scratch (no items, or every row fits one split) never
+  // looks the array up, so only calls that use it carry the first-call rule.
   void* scratch = nullptr;
-  const int rc = noalloc_scratch_address(&scratch);
-  if (rc != SEB_OK) return rc;
+  if (need > 0) {
+    const int rc = noalloc_scratch_address(&scratch);
+    if (rc != SEB_OK) return rc;
+  }
   return seb_paged_decode(q, q_stride_token, q_stride_head, k_cache, v_cache, num_blocks, block_table,
                           block_table_stride, max_blocks, q_starts, k_lens, q_pos_offsets, num_rows, total_query,
                           item_query, item_row, num_items, num_q_heads, num_kv_heads, head_dim, dtype, scale,
                           is_causal, blocks_per_split, out, out_stride_token, out_stride_head, lse,
-                          lse_stride_token, scratch, (int64_t)SEB_NOALLOC_SCRATCH_BYTES, err, stream);
+                          lse_stride_token, scratch, need > 0 ? (int64_t)SEB_NOALLOC_SCRATCH_BYTES : 0, err,
+                          stream);
 }

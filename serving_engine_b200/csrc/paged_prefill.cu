@@ -61,7 +61,12 @@ constexpr int kTmemCols = 512;
 constexpr int kColS = 0;
 constexpr int kColO = 256;
 constexpr float kLazyThreshold = 8.0f;
-constexpr int kSplitBelow = 256;
+// One 16-bit rounding of P costs up to about 0.013 / sqrt(visible keys) of
+// output error (8e-4 at 260 keys, 4e-4 at 1000), which next to the output's own
+// rounding (up to 9.8e-4 below |O| = 0.5 in bf16) would break a 2e-3 bound below
+// about a thousand keys; units whose first query sees fewer keys than this run
+// the remainder pass.
+constexpr int kSplitBelow = 1024;
 
 struct PrefillParams {
   int64_t num_blocks;
@@ -76,6 +81,13 @@ struct PrefillParams {
   const int32_t* rows;
   int32_t num_prefill_rows;
   int32_t mpairs;  // Q-tile pairs per row: ceil(max_q_len / (2 * queries_per_tile))
+  // Unit-list mode (units built on the device, seb_paged_attention): unit u is
+  // row unit_list[2u], kv head unit_list[2u+1] & 255, Q-tile pair
+  // unit_list[2u+1] >> 8, for u < *num_units (<= unit_cap). NULL: units come
+  // from rows x kv heads x mpairs as above.
+  const int32_t* unit_list;
+  const int32_t* num_units;
+  int32_t unit_cap;
   int32_t hq, hkv, group, qpt;  // qpt = queries per Q tile = 128 / group
   float scale_log2;
   int32_t causal;
@@ -180,15 +192,25 @@ __global__ void __launch_bounds__(kThreads, 1)
   int bx = blockIdx.x;
   const int half = bx & 1;
   bx >>= 1;
-  const int pr = p.mpairs - 1 - (bx % p.mpairs);
-  bx /= p.mpairs;
-  const int kvh = bx % p.hkv;
-  const int prow = bx / p.hkv;
-  if (prow >= p.num_prefill_rows) return;
-  const int row = p.rows ? __ldg(p.rows + prow) : prow;
-  if (row < 0 || row >= p.num_rows) {
-    if (threadIdx.x == 0 && kvh == 0 && pr == 0 && half == 0) atomic_or_err(p.err, SEB_ERRBIT_META);
-    return;
+  int pr, kvh, row;
+  if (p.unit_list) {
+    if (bx >= __ldg(p.num_units)) return;
+    row = __ldg(p.unit_list + 2 * bx);
+    const int e = __ldg(p.unit_list + 2 * bx + 1);
+    kvh = e & 255;
+    pr = e >> 8;
+    if (row < 0 || row >= p.num_rows) return;  // the list's builder reports bad rows
+  } else {
+    pr = p.mpairs - 1 - (bx % p.mpairs);
+    bx /= p.mpairs;
+    kvh = bx % p.hkv;
+    const int prow = bx / p.hkv;
+    if (prow >= p.num_prefill_rows) return;
+    row = p.rows ? __ldg(p.rows + prow) : prow;
+    if (row < 0 || row >= p.num_rows) {
+      if (threadIdx.x == 0 && kvh == 0 && pr == 0 && half == 0) atomic_or_err(p.err, SEB_ERRBIT_META);
+      return;
+    }
   }
   const int q_len = __ldg(p.q_lens + row);
   const int q_start = __ldg(p.q_starts + row);
@@ -622,12 +644,20 @@ struct PairUnit {
 
 // Decodes unit u; false: the unit does nothing (no such row or pair).
 __device__ __forceinline__ bool pair_unit(const PrefillParams& p, int u, PairUnit& w) {
-  const int pr = p.mpairs - 1 - (u % p.mpairs);
-  u /= p.mpairs;
-  w.kvh = u % p.hkv;
-  const int prow = u / p.hkv;
-  if (prow >= p.num_prefill_rows) return false;
-  w.row = p.rows ? __ldg(p.rows + prow) : prow;
+  int pr;
+  if (p.unit_list) {
+    w.row = __ldg(p.unit_list + 2 * u);
+    const int e = __ldg(p.unit_list + 2 * u + 1);
+    w.kvh = e & 255;
+    pr = e >> 8;
+  } else {
+    pr = p.mpairs - 1 - (u % p.mpairs);
+    u /= p.mpairs;
+    w.kvh = u % p.hkv;
+    const int prow = u / p.hkv;
+    if (prow >= p.num_prefill_rows) return false;
+    w.row = p.rows ? __ldg(p.rows + prow) : prow;
+  }
   if (w.row < 0 || w.row >= p.num_rows) return false;
   w.q_len = __ldg(p.q_lens + w.row);
   w.q_start = __ldg(p.q_starts + w.row);
@@ -660,11 +690,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
   const uint32_t crank = cluster_ctarank();
   const int cid = blockIdx.x >> 1;
   const int nclusters = gridDim.x >> 1;
-  const int units = p.num_prefill_rows * p.hkv * p.mpairs;
+  // Every thread of both CTAs reads the same unit count, so all roles walk the
+  // same units.
+  const int units = p.unit_list ? min(__ldg(p.num_units), p.unit_cap) : p.num_prefill_rows * p.hkv * p.mpairs;
   const int G = p.group;
 
-  // Metadata errors are reported once, by the cluster that owns the unit.
-  if (threadIdx.x == 0 && crank == 0) {
+  // Metadata errors are reported once, by the cluster that owns the unit (the
+  // builder of a unit list checks its rows itself).
+  if (threadIdx.x == 0 && crank == 0 && !p.unit_list) {
     for (int u = cid; u < units; u += nclusters) {
       const int prow = (u / p.mpairs) / p.hkv;
       const int row = p.rows ? __ldg(p.rows + prow) : prow;
@@ -1065,27 +1098,22 @@ template <typename T>
 int launch_prefill_pair(const PrefillParams& p, const void* q, int64_t q_st, int64_t q_sh, int total_query,
                         const void* kc, const void* vc, cudaStream_t s) {
   constexpr int smem = PairLayout::kBytes + 1024;
-  auto kern = prefill_pair_kernel<T>;
-  static bool attr_set[64] = {false};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-    SEB_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    attr_set[dev] = true;
-  }
+  constexpr auto kern = prefill_pair_kernel<T>;
+  int rc = set_smem_limit_once<kern>(smem);
+  if (rc != SEB_OK) return rc;
   const int dtype = std::is_same<T, __nv_bfloat16>::value ? SEB_BF16 : SEB_F16;
   CUtensorMap tq, tk, tv;
   const uint64_t qdims[3] = {128, (uint64_t)p.hq, (uint64_t)total_query};
   const uint64_t qstr[2] = {(uint64_t)q_sh * 2, (uint64_t)q_st * 2};
   const uint32_t qbox[3] = {64, (uint32_t)p.group, (uint32_t)p.qpt};
-  int rc = tensor_map_3d(&tq, q, dtype, qdims, qstr, qbox);
+  rc = tensor_map_3d(&tq, q, dtype, qdims, qstr, qbox);
   if (rc != SEB_OK) return rc;
   rc = kv_tensor_map(&tk, kc, dtype, p.num_blocks, p.hkv, 128);
   if (rc != SEB_OK) return rc;
   rc = kv_tensor_map(&tv, vc, dtype, p.num_blocks, p.hkv, 128);
   if (rc != SEB_OK) return rc;
   // persistent: one cluster per pair of SMs (or per unit, when there are fewer)
-  const int64_t units = (int64_t)p.num_prefill_rows * p.hkv * p.mpairs;
+  const int64_t units = p.unit_list ? (int64_t)p.unit_cap : (int64_t)p.num_prefill_rows * p.hkv * p.mpairs;
   const int64_t clusters = std::min<int64_t>(units, num_sms() / 2);
   kern<<<(unsigned)(2 * clusters), kPairThreads, smem, s>>>(p, tq, tk, tv);
   return launch_status("prefill_pair_kernel");
@@ -1096,48 +1124,41 @@ int launch_prefill(const PrefillParams& p, const void* q, int64_t q_st, int64_t 
                    const void* kc, const void* vc, cudaStream_t s) {
   using L = PrefillLayout<D>;
   constexpr int smem = L::kBytes + 1024;
-  auto kern = prefill_tc_kernel<T, D>;
-  static bool attr_set[64] = {false};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-    SEB_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    attr_set[dev] = true;
-  }
+  constexpr auto kern = prefill_tc_kernel<T, D>;
+  int rc = set_smem_limit_once<kern>(smem);
+  if (rc != SEB_OK) return rc;
   const int dtype = std::is_same<T, __nv_bfloat16>::value ? SEB_BF16 : SEB_F16;
   CUtensorMap tq, tk, tv;
   const uint64_t qdims[3] = {(uint64_t)D, (uint64_t)p.hq, (uint64_t)total_query};
   const uint64_t qstr[2] = {(uint64_t)q_sh * 2, (uint64_t)q_st * 2};
   const uint32_t qbox[3] = {64, (uint32_t)p.group, (uint32_t)p.qpt};
-  int rc = tensor_map_3d(&tq, q, dtype, qdims, qstr, qbox);
+  rc = tensor_map_3d(&tq, q, dtype, qdims, qstr, qbox);
   if (rc != SEB_OK) return rc;
   rc = kv_tensor_map(&tk, kc, dtype, p.num_blocks, p.hkv, D);
   if (rc != SEB_OK) return rc;
   rc = kv_tensor_map(&tv, vc, dtype, p.num_blocks, p.hkv, D);
   if (rc != SEB_OK) return rc;
-  const int64_t grid = (int64_t)p.num_prefill_rows * p.hkv * p.mpairs * 2;
+  const int64_t grid = (p.unit_list ? (int64_t)p.unit_cap : (int64_t)p.num_prefill_rows * p.hkv * p.mpairs) * 2;
   kern<<<(unsigned)grid, kThreads, smem, s>>>(p, tq, tk, tv);
   return launch_status("prefill_tc_kernel");
 }
 
 }  // namespace
-}  // namespace seb
 
-extern "C" int seb_paged_prefill(const void* q, int64_t q_stride_token, int64_t q_stride_head, const void* k_cache,
-                                 const void* v_cache, int64_t num_blocks, const int32_t* block_table,
-                                 int64_t block_table_stride, int64_t max_blocks, const int32_t* q_starts,
-                                 const int32_t* q_lens, const int32_t* k_lens, const int32_t* q_pos_offsets,
-                                 int32_t num_rows, int32_t total_query, const int32_t* rows,
-                                 int32_t num_prefill_rows, int32_t max_q_len, int32_t num_q_heads,
-                                 int32_t num_kv_heads, int32_t head_dim, int32_t dtype, float scale,
-                                 int32_t is_causal, void* out, int64_t out_stride_token, int64_t out_stride_head,
-                                 float* lse, int64_t lse_stride_token, int32_t* err, void* stream) {
-  using namespace seb;
-  clear_error();
+int paged_prefill_impl(const void* q, int64_t q_stride_token, int64_t q_stride_head, const void* k_cache,
+                       const void* v_cache, int64_t num_blocks, const int32_t* block_table,
+                       int64_t block_table_stride, int64_t max_blocks, const int32_t* q_starts,
+                       const int32_t* q_lens, const int32_t* k_lens, const int32_t* q_pos_offsets, int32_t num_rows,
+                       int32_t total_query, const int32_t* rows, int32_t num_prefill_rows, int32_t max_q_len,
+                       int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim, int32_t dtype, float scale,
+                       int32_t is_causal, void* out, int64_t out_stride_token, int64_t out_stride_head, float* lse,
+                       int64_t lse_stride_token, int32_t* err, void* stream, const int32_t* unit_list,
+                       const int32_t* num_units, int32_t unit_cap) {
   SEB_CHECK_ARG(dtype == SEB_BF16 || dtype == SEB_F16, "seb_paged_prefill: bf16 or fp16 required (dtype %d)", dtype);
-  SEB_CHECK_ARG(num_prefill_rows >= 0 && num_rows >= 0 && total_query >= 0 && max_q_len >= 0,
+  SEB_CHECK_ARG(num_prefill_rows >= 0 && num_rows >= 0 && total_query >= 0 && max_q_len >= 0 && unit_cap >= 0,
                 "seb_paged_prefill: negative count");
-  if (num_prefill_rows == 0 || max_q_len == 0) return SEB_OK;
+  SEB_CHECK_ARG((unit_list == nullptr) == (num_units == nullptr), "seb_paged_prefill: unit list without its count");
+  if (unit_list ? unit_cap == 0 : (num_prefill_rows == 0 || max_q_len == 0)) return SEB_OK;
   SEB_CHECK_ARG(num_q_heads > 0 && num_kv_heads > 0 && num_q_heads % num_kv_heads == 0,
                 "seb_paged_prefill: num_q_heads (%d) must be a positive multiple of num_kv_heads (%d)", num_q_heads,
                 num_kv_heads);
@@ -1186,7 +1207,10 @@ extern "C" int seb_paged_prefill(const void* q, int64_t q_stride_token, int64_t 
   p.lse = lse;
   p.lse_st = lse_stride_token;
   p.err = err;
-  const int64_t grid = (int64_t)num_prefill_rows * num_kv_heads * p.mpairs * 2;
+  p.unit_list = unit_list;
+  p.num_units = num_units;
+  p.unit_cap = unit_list ? unit_cap : 0;
+  const int64_t grid = (unit_list ? (int64_t)unit_cap : (int64_t)num_prefill_rows * num_kv_heads * p.mpairs) * 2;
   SEB_CHECK_ARG(grid < (1ll << 31), "seb_paged_prefill: grid too large");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   // head_dim 128: the CTA-pair kernel; head_dim 64: one CTA per pair of Q tiles
@@ -1199,4 +1223,23 @@ extern "C" int seb_paged_prefill(const void* q, int64_t q_stride_token, int64_t 
   return head_dim == 128
              ? launch_prefill_pair<__half>(p, q, q_stride_token, q_stride_head, total_query, k_cache, v_cache, s)
              : launch_prefill<__half, 64>(p, q, q_stride_token, q_stride_head, total_query, k_cache, v_cache, s);
+}
+
+}  // namespace seb
+
+extern "C" int seb_paged_prefill(const void* q, int64_t q_stride_token, int64_t q_stride_head, const void* k_cache,
+                                 const void* v_cache, int64_t num_blocks, const int32_t* block_table,
+                                 int64_t block_table_stride, int64_t max_blocks, const int32_t* q_starts,
+                                 const int32_t* q_lens, const int32_t* k_lens, const int32_t* q_pos_offsets,
+                                 int32_t num_rows, int32_t total_query, const int32_t* rows,
+                                 int32_t num_prefill_rows, int32_t max_q_len, int32_t num_q_heads,
+                                 int32_t num_kv_heads, int32_t head_dim, int32_t dtype, float scale,
+                                 int32_t is_causal, void* out, int64_t out_stride_token, int64_t out_stride_head,
+                                 float* lse, int64_t lse_stride_token, int32_t* err, void* stream) {
+  seb::clear_error();
+  return seb::paged_prefill_impl(q, q_stride_token, q_stride_head, k_cache, v_cache, num_blocks, block_table,
+                                 block_table_stride, max_blocks, q_starts, q_lens, k_lens, q_pos_offsets, num_rows,
+                                 total_query, rows, num_prefill_rows, max_q_len, num_q_heads, num_kv_heads,
+                                 head_dim, dtype, scale, is_causal, out, out_stride_token, out_stride_head, lse,
+                                 lse_stride_token, err, stream, nullptr, nullptr, 0);
 }

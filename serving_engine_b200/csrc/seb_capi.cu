@@ -17,16 +17,16 @@ void set_error(const char* fmt, ...) {
 void clear_error() { g_last_error[0] = 0; }
 
 int num_sms() {
-  static int cache[64] = {0};
+  static std::atomic<int> cache[64];
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
-  if (cache[dev] == 0) {
-    int n = 0;
+  int n = cache[dev].load(std::memory_order_relaxed);
+  if (n == 0) {
     if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
       n = 148;
-    cache[dev] = n;
+    cache[dev].store(n, std::memory_order_relaxed);
   }
-  return cache[dev];
+  return n;
 }
 
 }  // namespace seb

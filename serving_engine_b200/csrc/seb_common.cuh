@@ -8,8 +8,10 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
 #include <cstdarg>
 #include <cstdio>
+#include <mutex>
 
 #include "../../include/serving_engine_b200.h"
 
@@ -61,6 +63,30 @@ inline bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintp
 
 // Number of SMs of the current device (cached per device id).
 int num_sms();
+
+// Raises Kernel's dynamic shared-memory limit to `bytes` once per device (the
+// attribute is per device context). Safe when several host threads launch at
+// once: the first caller per device sets it under a lock, later callers see the
+// published flag.
+template <auto Kernel>
+int set_smem_limit_once(int bytes) {
+  constexpr int kMaxDevices = 64;
+  static std::atomic<bool> done[kMaxDevices];
+  static std::mutex mu;
+  int dev = 0;
+  SEB_CHECK_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= kMaxDevices) {
+    SEB_CHECK_CUDA(cudaFuncSetAttribute(Kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+    return SEB_OK;
+  }
+  if (done[dev].load(std::memory_order_acquire)) return SEB_OK;
+  std::lock_guard<std::mutex> lk(mu);
+  if (!done[dev].load(std::memory_order_relaxed)) {
+    SEB_CHECK_CUDA(cudaFuncSetAttribute(Kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+    done[dev].store(true, std::memory_order_release);
+  }
+  return SEB_OK;
+}
 
 // ------------------------------------------------------------- element traits
 template <typename T> struct Elem;
@@ -288,5 +314,31 @@ __device__ __forceinline__ float warp_sum_xor(float v, int lanemask_lo, int lane
   for (int o = lanemask_lo; o <= lanemask_hi; o <<= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
   return v;
 }
+
+// ------------------------------------------------- launchers shared across files
+// seb_paged_decode with an optional device-side item count: items at or past
+// *num_items_dev (num_items bounds it and sizes the grid) exit at once.
+int paged_decode_impl(const void* q, int64_t q_stride_token, int64_t q_stride_head, const void* k_cache,
+                      const void* v_cache, int64_t num_blocks, const int32_t* block_table, int64_t block_table_stride,
+                      int64_t max_blocks, const int32_t* q_starts, const int32_t* k_lens, const int32_t* q_pos_offsets,
+                      int32_t num_rows, int32_t total_query, const int32_t* item_query, const int32_t* item_row,
+                      int32_t num_items, const int32_t* num_items_dev, int32_t num_q_heads, int32_t num_kv_heads,
+                      int32_t head_dim, int32_t dtype, float scale, int32_t is_causal, int32_t blocks_per_split,
+                      void* out, int64_t out_stride_token, int64_t out_stride_head, float* lse,
+                      int64_t lse_stride_token, void* workspace, int64_t workspace_bytes, int32_t* err,
+                      void* stream);
+
+// seb_paged_prefill with an optional device-built unit list: unit u < *num_units
+// (<= unit_cap, which sizes the grid) is row unit_list[2u], kv head
+// unit_list[2u+1] & 255 and Q-tile pair unit_list[2u+1] >> 8.
+int paged_prefill_impl(const void* q, int64_t q_stride_token, int64_t q_stride_head, const void* k_cache,
+                       const void* v_cache, int64_t num_blocks, const int32_t* block_table,
+                       int64_t block_table_stride, int64_t max_blocks, const int32_t* q_starts,
+                       const int32_t* q_lens, const int32_t* k_lens, const int32_t* q_pos_offsets, int32_t num_rows,
+                       int32_t total_query, const int32_t* rows, int32_t num_prefill_rows, int32_t max_q_len,
+                       int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim, int32_t dtype, float scale,
+                       int32_t is_causal, void* out, int64_t out_stride_token, int64_t out_stride_head, float* lse,
+                       int64_t lse_stride_token, int32_t* err, void* stream, const int32_t* unit_list,
+                       const int32_t* num_units, int32_t unit_cap);
 
 }  // namespace seb

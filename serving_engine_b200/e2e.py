@@ -1,34 +1,45 @@
-"""End-to-end continuous-batching driver over a Hugging Face Llama model.
+"""End-to-end continuous batching over a Hugging Face Llama model.
 
 The serving engine's own Scheduler / BlockManager / LLMEngine (serving_engine/
 scheduler.py, block_manager.py, engine.py) stay the product path and call this
 backend through the registered "paged|b200" attention function. They are not
-part of this package, so this module carries a compact driver with the same
-per-step semantics, used to measure end-to-end throughput and greedy-token
-parity on machines where the engine package is not installed:
+part of this package and cannot travel to a GPU machine without the engine
+checkout, so this module carries a driver that reproduces their decisions step
+for step, used to measure end-to-end throughput and to check greedy-token
+parity against the reference engine's recorded runs:
 
-* running requests before waiting ones; a decode row costs one token and gets
-  a new block when its table is full (block_manager.py:89-115);
-* waiting requests are admitted first-come-first-served while blocks for their
-  whole prompt are free and the token budget has room; prefill is chunked to
-  the budget left (scheduler.py:55-149);
+* ``BlockPool`` keeps the BlockManager's rules (block_manager.py:7-141): a free
+  list taken from its end, per-block reference counts, chained-hash prefix
+  matching of full prompt blocks at admission, first-writer-wins registration
+  of computed blocks, delta allocation of a request's whole length, one block
+  per decode step when the table is full, release with hash invalidation;
+* ``Scheduler`` keeps the per-step admission rules (scheduler.py:55-184):
+  running requests before waiting ones, a token budget that only limits work
+  piled on top of something already batched (a lone candidate always fits), the
+  optional chunk floor, prefill chunks filling the budget left, and, when
+  nothing at all could be scheduled while a decode row waits for a block, the
+  eviction of the most recently admitted other running request (its blocks are
+  freed and it is recomputed from scratch later);
 * one model call per step over the flattened batch: per-token write slots
   block_table[pos // 16] * 16 + pos % 16 (model_runner.py:127-129, :149-170),
-  the step metadata of build_paged_batch_metadata, last-token logits per row,
-  greedy argmax; a request that finished its final prefill chunk emits its
-  first token (engine.py:92-116).
+  the step metadata of build_paged_batch_metadata, greedy argmax of each row's
+  last-token logits; a decode row, or a prefill row whose chunk completes its
+  prompt, emits a token (engine.py:92-116).
 
 Unlike the reference, logits are computed for the last token of each row only
 (logits_to_keep), argmax runs on the device, and all next tokens come back in
-one device-to-host copy; preemption is not modelled (the pool is sized to fit).
-With use_graphs, decode-only steps replay a CUDA graph captured per padded
+one device-to-host copy. A prefill row whose whole prompt was matched in the
+prefix cache (a chunk of 0 tokens) runs its last token again, which rewrites
+the same K/V; the reference reads an unrelated row's logits there. With
+use_graphs, decode-only steps replay a CUDA graph captured per padded
 batch-size bucket: the step's tokens, positions, slots, lengths and block
 tables go to fixed device buffers in two host-to-device copies, and pad rows
-attend over a reserved scratch block.
+attend over a scratch block placed after the engine's blocks.
 """
 from __future__ import annotations
 
 import math
+import time
 from dataclasses import dataclass, field
 
 import numpy as np
@@ -42,37 +53,232 @@ BLOCK_SIZE = 16
 
 @dataclass
 class Seq:
+    """One request (serving_engine/request.py:27-64)."""
+
     rid: int
     prompt: list
     max_new: int
+    eos: int | None = None
     out: list = field(default_factory=list)
     table: list = field(default_factory=list)
     computed: int = 0
-    prefilling: bool = True
-    finished: bool = False
-    tab: np.ndarray | None = None  # block table as a fixed-width int32 row (graph path)
+    decoding: bool = False           # phase: prefill until its last chunk ran
+    status: str = "waiting"          # waiting | running | preempted | finished
+    preemptions: int = 0
 
     @property
     def total_len(self) -> int:
         return len(self.prompt) + len(self.out)
 
+    def tokens(self) -> list:
+        return self.prompt + self.out
+
+
+class BlockPool:
+    """Block ids, reference counts and the chained-hash prefix cache."""
+
+    def __init__(self, num_blocks: int, block_size: int = BLOCK_SIZE):
+        self.block_size = block_size
+        self.free_ids = list(range(num_blocks))
+        self.refs = [0] * num_blocks
+        self.block_hash: list[int | None] = [None] * num_blocks
+        self.by_hash: dict[int, int] = {}
+
+    @property
+    def num_free(self) -> int:
+        return len(self.free_ids)
+
+    def _take(self, s: Seq) -> None:
+        bid = self.free_ids.pop()
+        s.table.append(bid)
+        self.refs[bid] += 1
+
+    def match_prefix(self, s: Seq) -> None:
+        """Share the cached blocks of the prompt's longest cached run of full blocks."""
+        parent = None
+        for i in range(len(s.prompt) // self.block_size):
+            h = hash((parent, tuple(s.prompt[i * self.block_size:(i + 1) * self.block_size])))
+            bid = self.by_hash.get(h)
+            if bid is None:
+                break
+            s.table.append(bid)
+            self.refs[bid] += 1
+            parent = h
+        s.computed = len(s.table) * self.block_size
+
+    def shortfall(self, s: Seq) -> int:
+        """Blocks still missing for the request's whole current length."""
+        return -(-s.total_len // self.block_size) - len(s.table)
+
+    def can_claim(self, s: Seq) -> bool:
+        return self.shortfall(s) <= self.num_free
+
+    def claim(self, s: Seq) -> None:
+        for _ in range(self.shortfall(s)):
+            self._take(s)
+
+    def register(self, s: Seq) -> None:
+        """Hash the prompt blocks that are now fully computed (first writer wins)."""
+        parent = None
+        for i in range(min(s.computed, len(s.prompt)) // self.block_size):
+            bid = s.table[i]
+            if self.block_hash[bid] is not None:
+                parent = self.block_hash[bid]
+                continue
+            h = hash((parent, tuple(s.prompt[i * self.block_size:(i + 1) * self.block_size])))
+            if h not in self.by_hash:
+                self.by_hash[h] = bid
+                self.block_hash[bid] = h
+            parent = h
+
+    def covers(self, s: Seq) -> bool:
+        return len(s.table) * self.block_size >= s.total_len
+
+    def can_grow(self, s: Seq) -> bool:
+        return self.covers(s) or self.num_free >= 1
+
+    def grow(self, s: Seq) -> None:
+        if not self.covers(s):
+            self._take(s)
+
+    def release(self, s: Seq) -> None:
+        for bid in s.table:
+            self.refs[bid] -= 1
+            if self.refs[bid] == 0:
+                self.free_ids.append(bid)
+                h = self.block_hash[bid]
+                if h is not None:
+                    del self.by_hash[h]
+                    self.block_hash[bid] = None
+        s.table = []
+
+    def preempt(self, s: Seq) -> None:
+        self.release(s)
+        s.computed = 0
+        s.decoding = False
+        s.status = "preempted"
+        s.preemptions += 1
+
+
+@dataclass
+class StepPlan:
+    rows: list = field(default_factory=list)        # (seq, chunk); chunk None = decode row
+    final: set = field(default_factory=set)         # rids whose chunk completes the prefill
+    preempted: list = field(default_factory=list)   # seqs evicted this step
+
+
+class Scheduler:
+    """Per-step admission over a BlockPool (running before waiting)."""
+
+    def __init__(self, pool: BlockPool, max_num_batched_tokens: int | None = None,
+                 max_num_seqs: int | None = None, min_chunk_size: int | None = None):
+        self.pool = pool
+        self.max_tokens = max_num_batched_tokens
+        self.max_seqs = max_num_seqs
+        self.min_chunk = min_chunk_size
+        self.waiting: list[Seq] = []
+        self.running: list[Seq] = []
+
+    def add(self, s: Seq) -> None:
+        self.pool.match_prefix(s)
+        self.waiting.append(s)
+
+    def _fits(self, batched: int, cost: int) -> bool:
+        # the budget limits only work piled on top of something already batched
+        return self.max_tokens is None or batched == 0 or batched + cost <= self.max_tokens
+
+    def plan(self) -> StepPlan:
+        plan = StepPlan()
+        blocked: list[Seq] = []
+        batched = 0
+        for s in self.running + self.waiting:
+            if self.max_seqs is not None and len(plan.rows) >= self.max_seqs:
+                break
+            left = s.total_len - s.computed
+            if s.decoding:
+                if not self._fits(batched, 1):
+                    continue
+                if not self.pool.can_grow(s):
+                    blocked.append(s)
+                    continue
+                self.pool.grow(s)
+                plan.rows.append((s, None))
+                batched += 1
+                continue
+            if not self._fits(batched, left if self.min_chunk is None else min(self.min_chunk, left)):
+                continue
+            admitted = s.status == "running"
+            if not admitted and not self.pool.can_claim(s):
+                continue
+            chunk = left if self.max_tokens is None else min(left, self.max_tokens - batched)
+            if not admitted:
+                self.pool.claim(s)
+                s.status = "running"
+                self.waiting = [w for w in self.waiting if w is not s]
+                self.running.append(s)
+            plan.rows.append((s, chunk))
+            if s.computed + chunk >= s.total_len:
+                plan.final.add(s.rid)
+            batched += chunk
+        if not plan.rows and blocked:
+            # nothing advanced and a decode row waits for a block: evict the most
+            # recently admitted other running request and retry the first one
+            retry = blocked[0]
+            victim = next((r for r in reversed(self.running) if r is not retry), None)
+            if victim is not None:
+                self.pool.preempt(victim)
+                self.running.remove(victim)
+                self.waiting.append(victim)
+                plan.preempted.append(victim)
+                if self.pool.can_grow(retry):
+                    self.pool.grow(retry)
+                    plan.rows.append((retry, None))
+        return plan
+
+    def commit(self, plan: StepPlan) -> list[Seq]:
+        """Bookkeeping after the step's tokens were appended; returns the requests
+        that finished."""
+        finished = []
+        for s, chunk in plan.rows:
+            if s.out and (len(s.out) >= s.max_new or (s.eos is not None and s.out[-1] == s.eos)):
+                s.status = "finished"
+                self.pool.release(s)
+                self.running = [r for r in self.running if r is not s]
+                finished.append(s)
+            elif not s.decoding:
+                s.computed += chunk
+                self.pool.register(s)
+                if s.rid in plan.final:
+                    s.decoding = True
+        return finished
+
+    def has_unfinished(self) -> bool:
+        return bool(self.waiting or self.running)
+
 
 @dataclass
 class StepStats:
-    kind: str          # "decode", "prefill" or "mixed"
+    kind: str          # "decode", "prefill", "mixed" or "idle"
     tokens: int        # query tokens in the step
     new_tokens: int    # sampled tokens emitted
     seconds: float
 
 
 class E2EEngine:
-    """Continuous batching over `model` (a LlamaForCausalLM on a CUDA device)."""
+    """Continuous batching over `model` (a LlamaForCausalLM on a CUDA device).
+
+    num_blocks, max_num_batched_tokens, max_num_seqs and min_chunk_size mean what
+    they mean for the reference's LLMEngine (engine.py:18-61). ``trace`` records
+    every step's schedule: per row (request id, "P" or "D", chunk, computed
+    tokens before the step, block table) and the ids preempted.
+    """
 
     GRAPH_BUCKETS = (1, 2, 4, 8, 16, 32, 64, 128, 256)
 
-    def __init__(self, model, num_blocks: int, max_num_batched_tokens: int = 8192, max_num_seqs: int = 256,
+    def __init__(self, model, num_blocks: int, max_num_batched_tokens: int | None = None,
+                 max_num_seqs: int | None = None, min_chunk_size: int | None = None,
                  attn_implementation: str = PAGED_B200_ATTN_IMPL, use_graphs: bool = False,
-                 max_context: int = 8192):
+                 max_context: int = 8192, record_logits: bool = False):
         if attn_implementation == PAGED_B200_ATTN_IMPL:
             register()
         model.set_attn_implementation(attn_implementation)
@@ -81,104 +287,75 @@ class E2EEngine:
         self.device = next(model.parameters()).device
         self.dtype = next(model.parameters()).dtype
         head_dim = getattr(cfg, "head_dim", None) or cfg.hidden_size // cfg.num_attention_heads
-        self.kv_cache = torch.zeros(cfg.num_hidden_layers, 2, num_blocks, BLOCK_SIZE, cfg.num_key_value_heads,
-                                    head_dim, dtype=self.dtype, device=self.device)
+        # with graphs, one extra block after the engine's blocks is the target of pad rows
+        self.kv_cache = torch.zeros(cfg.num_hidden_layers, 2, num_blocks + (1 if use_graphs else 0), BLOCK_SIZE,
+                                    cfg.num_key_value_heads, head_dim, dtype=self.dtype, device=self.device)
         self.cache = PagedKVCache(self.kv_cache)
         self.use_graphs = use_graphs
         self.width = -(-max_context // BLOCK_SIZE)
-        # the last block is reserved as the target of padded graph rows
-        self.scratch_block = num_blocks - 1 if use_graphs else None
-        self.free = list(range(num_blocks - 1 if use_graphs else num_blocks))
+        self.scratch_block = num_blocks if use_graphs else None
         self.num_blocks = num_blocks
+        self.pool = BlockPool(num_blocks)
+        self.sched = Scheduler(self.pool, max_num_batched_tokens, max_num_seqs, min_chunk_size)
         self.graphs: dict[int, dict] = {}
-        self.max_tokens = max_num_batched_tokens
-        self.max_seqs = max_num_seqs
-        self.waiting: list[Seq] = []
-        self.running: list[Seq] = []
+        self.seqs: list[Seq] = []
         self.done: list[Seq] = []
         self.stats: list[StepStats] = []
-        self._next_id = 0
+        self.trace: list[dict] = []
+        self.record_logits = record_logits
+        self.logit_log: list[tuple] = []  # (rid, output index, top-5 ids, top-5 logits) when recording
 
-    def add_request(self, prompt_token_ids, max_new_tokens: int) -> int:
-        s = Seq(self._next_id, list(prompt_token_ids), max_new_tokens)
-        self._next_id += 1
-        self.waiting.append(s)
+    @property
+    def free(self) -> list:
+        return self.pool.free_ids
+
+    def add_request(self, prompt_token_ids, max_new_tokens: int, eos_token_id: int | None = None) -> int:
+        s = Seq(len(self.seqs), list(prompt_token_ids), max_new_tokens, eos_token_id)
+        self.seqs.append(s)
+        self.sched.add(s)
         return s.rid
-
-    # ----------------------------------------------------------- scheduling
-    def _set_blocks(self, s: Seq, blocks) -> None:
-        s.table = list(blocks)
-        if self.use_graphs:
-            if len(s.table) > self.width:
-                raise ValueError(f"request of {s.total_len} tokens exceeds max_context {self.width * BLOCK_SIZE}")
-            s.tab = np.zeros(self.width, dtype=np.int32)
-            s.tab[:len(s.table)] = s.table
-
-    def _append_block(self, s: Seq, bid: int) -> None:
-        s.table.append(bid)
-        if self.use_graphs:
-            if len(s.table) > self.width:
-                raise ValueError(f"request exceeds max_context {self.width * BLOCK_SIZE}")
-            s.tab[len(s.table) - 1] = bid
-
-    def _blocks_for(self, n_tokens: int) -> int:
-        return -(-n_tokens // BLOCK_SIZE)
-
-    def _schedule(self):
-        rows = []  # (seq, chunk) ; chunk 0 = decode
-        budget = self.max_tokens
-        for s in self.running:
-            if len(rows) >= self.max_seqs:
-                break
-            if s.prefilling:
-                continue
-            if len(s.table) * BLOCK_SIZE < s.total_len:
-                if not self.free:
-                    continue
-                self._append_block(s, self.free.pop())
-            rows.append((s, 0))
-            budget -= 1
-        for s in self.running:
-            if len(rows) >= self.max_seqs or budget <= 0:
-                break
-            if s.prefilling:
-                chunk = min(s.total_len - s.computed, budget)
-                rows.append((s, chunk))
-                budget -= chunk
-        while self.waiting and len(rows) < self.max_seqs and budget > 0:
-            s = self.waiting[0]
-            need = self._blocks_for(s.total_len)
-            if need > len(self.free):
-                break
-            self.waiting.pop(0)
-            self._set_blocks(s, [self.free.pop() for _ in range(need)])
-            self.running.append(s)
-            chunk = min(s.total_len - s.computed, budget)
-            rows.append((s, chunk))
-            budget -= chunk
-        return rows
 
     # ----------------------------------------------------------------- step
     @torch.inference_mode()
     def step(self) -> int:
         """One engine iteration; returns the number of tokens sampled."""
-        import time
-
-        rows = self._schedule()
-        if not rows:
-            return 0
         t0 = time.perf_counter()
-        if self.graphs and all(c == 0 for _, c in rows) and len(rows) <= max(self.graphs):
-            return self._finish_step(rows, self._graph_decode(rows), t0, len(rows))
+        plan = self.sched.plan()
+        self.trace.append({
+            "rows": [[s.rid, "D" if c is None else "P", 0 if c is None else c, s.computed, list(s.table)]
+                     for s, c in plan.rows],
+            "preempted": [s.rid for s in plan.preempted]})
+        if not plan.rows:
+            self.stats.append(StepStats("idle", 0, 0, time.perf_counter() - t0))
+            return 0
+        n_tokens = sum(1 if c is None else max(c, 1) for _, c in plan.rows)
+        if (self.graphs and not self.record_logits and all(c is None for _, c in plan.rows)
+                and len(plan.rows) <= max(self.graphs)):
+            next_tok = self._graph_decode(plan.rows)
+        else:
+            next_tok = self._eager_step(plan.rows)
+        emitted = 0
+        for (s, c), tok in zip(plan.rows, next_tok):
+            if c is None or s.rid in plan.final:
+                s.out.append(int(tok))
+                emitted += 1
+        for s in self.sched.commit(plan):
+            self.done.append(s)
+        kinds = {"decode" if c is None else "prefill" for _, c in plan.rows}
+        self.stats.append(StepStats("mixed" if len(kinds) > 1 else kinds.pop(), n_tokens, emitted,
+                                    time.perf_counter() - t0))
+        return emitted
+
+    def _eager_step(self, rows) -> list:
         toks, pos, slots = [], [], []
         q_lens, k_lens, q_pos = [], [], []
         for s, chunk in rows:
-            if chunk == 0:  # decode: the newest token at position total_len - 1
+            seq_toks = s.tokens()
+            if chunk is None or chunk == 0:  # the newest token (a decode row, or a fully cached prompt)
                 p0, n = s.total_len - 1, 1
-                toks.append(s.out[-1])
+                toks.append(seq_toks[-1])
             else:
                 p0, n = s.computed, chunk
-                seq_toks = s.prompt + s.out
                 toks.extend(seq_toks[p0:p0 + n])
             positions = np.arange(p0, p0 + n)
             table = np.asarray(s.table, dtype=np.int64)
@@ -197,36 +374,14 @@ class E2EEngine:
         out = self.model(input_ids=ids.unsqueeze(0), position_ids=pos_t.unsqueeze(0), attention_mask=None,
                          past_key_values=None, use_cache=False, cache=self.cache, write_index=slot_t,
                          paged_metadata=md, logits_to_keep=last)
-        next_tok = out.logits[0].argmax(dim=-1).tolist()
-        return self._finish_step(rows, next_tok, t0, len(toks))
-
-    def _finish_step(self, rows, next_tok, t0, n_tokens) -> int:
-        import time
-
-        emitted = 0
-        for (s, chunk), tok in zip(rows, next_tok):
-            if chunk == 0:
-                s.out.append(tok)
-                emitted += 1
-            else:
-                s.computed += chunk
-                if s.computed >= s.total_len:
-                    s.prefilling = False
-                    s.out.append(tok)
-                    emitted += 1
-            if not s.prefilling and len(s.out) >= s.max_new:
-                s.finished = True
-        for s, _ in rows:
-            if s.finished and s in self.running:
-                self.running.remove(s)
-                self.free.extend(s.table)
-                s.table = []
-                s.tab = None
-                self.done.append(s)
-        kinds = {"decode" if c == 0 else "prefill" for _, c in rows}
-        self.stats.append(StepStats("mixed" if len(kinds) > 1 else kinds.pop(), n_tokens, emitted,
-                                    time.perf_counter() - t0))
-        return emitted
+        logits = out.logits[0]
+        if self.record_logits:
+            top = torch.topk(logits.float(), 5, dim=-1)
+            ids5, vals5 = top.indices.tolist(), top.values.tolist()
+            for i, (s, c) in enumerate(rows):
+                if c is None or (s.computed + c >= s.total_len):
+                    self.logit_log.append((s.rid, len(s.out), ids5[i], vals5[i]))
+        return logits.argmax(dim=-1).tolist()
 
     # ------------------------------------------------------------ CUDA graphs
     def _graph_inputs(self, bucket: int) -> dict:
@@ -239,7 +394,6 @@ class E2EEngine:
 
     def _load_graph_inputs(self, st: dict, rows) -> None:
         """Real rows first, then pad rows on the scratch block."""
-        b = len(rows)
         bucket = st["last"].numel()
         h = st["host"].numpy()
         k_lens = np.ones(bucket, dtype=np.int32)
@@ -249,13 +403,14 @@ class E2EEngine:
         h[1, :] = 0
         h[2, :] = self.scratch_block * BLOCK_SIZE
         for i, (s, _) in enumerate(rows):
+            if len(s.table) > self.width:
+                raise ValueError(f"request of {s.total_len} tokens exceeds max_context {self.width * BLOCK_SIZE}")
             p = s.total_len - 1
+            tables[i, :len(s.table)] = s.table
             h[0, i] = s.out[-1]
             h[1, i] = p
-            h[2, i] = s.tab[p // BLOCK_SIZE] * BLOCK_SIZE + p % BLOCK_SIZE
+            h[2, i] = s.table[p // BLOCK_SIZE] * BLOCK_SIZE + p % BLOCK_SIZE
             k_lens[i] = s.total_len
-        if b:
-            tables[:b] = np.stack([s.tab for s, _ in rows])
         st["dev"].copy_(st["host"], non_blocking=True)
         st["md"].update(k_lens, tables)
 
@@ -272,7 +427,8 @@ class E2EEngine:
         the decode workspace is allocated at its largest size before capture)."""
         if not self.use_graphs:
             raise RuntimeError("engine built without use_graphs")
-        buckets = sorted(buckets or [b for b in self.GRAPH_BUCKETS if b <= self.max_seqs], reverse=True)
+        limit = self.sched.max_seqs or max(self.GRAPH_BUCKETS)
+        buckets = sorted(buckets or [b for b in self.GRAPH_BUCKETS if b <= limit], reverse=True)
         pool = torch.cuda.graph_pool_handle()
         side = torch.cuda.Stream(device=self.device)
         for bucket in buckets:
@@ -299,12 +455,17 @@ class E2EEngine:
         return st["out"][:len(rows)].tolist()
 
     def has_unfinished(self) -> bool:
-        return bool(self.waiting or self.running)
+        return self.sched.has_unfinished()
 
-    def run(self) -> None:
+    def run(self, max_idle_steps: int = 1000) -> None:
+        idle = 0
         while self.has_unfinished():
-            if self.step() == 0 and not self.running and self.waiting:
-                raise RuntimeError("pool too small for the next request")
+            if self.step() == 0 and not self.trace[-1]["rows"]:
+                idle += 1
+                if idle > max_idle_steps:
+                    raise RuntimeError("no request can be scheduled: the pool is too small")
+            else:
+                idle = 0
 
 
 def llama_config(name: str):
@@ -322,12 +483,20 @@ def llama_config(name: str):
     raise ValueError(name)
 
 
-def random_llama(name: str, seed: int, dtype=torch.float32, device="cpu"):
-    """Seeded random-init LlamaForCausalLM: identical weights for the same seed on
-    every machine with this torch build (initialised on the CPU, then moved)."""
+def random_llama(name: str, seed: int, dtype=torch.float32, device="cpu", init_on_device: bool = False):
+    """Seeded random-init LlamaForCausalLM. By default the weights are initialised
+    on the CPU, then moved: identical weights for the same seed on every machine
+    with this torch build (what the parity fixtures rely on). init_on_device
+    initialises directly on `device` (much faster for the large shapes; other
+    values than the CPU initialisation gives)."""
     from transformers import LlamaForCausalLM
 
     torch.manual_seed(seed)
+    if init_on_device:
+        torch.cuda.manual_seed(seed)
+        with torch.device(device):
+            model = LlamaForCausalLM(llama_config(name))
+        return model.to(dtype=dtype).eval()
     model = LlamaForCausalLM(llama_config(name))
     return model.to(device=device, dtype=dtype).eval()
 

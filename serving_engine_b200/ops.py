@@ -312,6 +312,69 @@ def paged_decode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, 
     return out, lse
 
 
+# ------------------------------------------- whole batch, device-side routing
+@_nvtx
+def paged_attention_routed(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, block_table: torch.Tensor,
+                           q_lens: torch.Tensor, k_lens: torch.Tensor, q_starts: torch.Tensor,
+                           q_pos_offsets: torch.Tensor, num_q_heads: int, num_kv_heads: int, scale: float,
+                           is_causal: bool = True, out: torch.Tensor | None = None,
+                           lse: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor]:
+    """Paged attention for a mixed batch described only by the reference's
+    per-row device arrays (q_lens, k_lens, q_starts, q_pos_offsets, block_table:
+    the dict of build_paged_batch_metadata). The rows are split into decode items
+    and tcgen05 prefill units on the device (seb_paged_attention); the host reads
+    nothing back."""
+    dev = _require_cuda("paged_attention_routed", q, k_cache, v_cache, block_table, q_lens, k_lens, q_starts,
+                        q_pos_offsets)
+    if q.dim() != 3 or q.stride(2) != 1 or q.shape[1] != num_q_heads:
+        raise ValueError(f"paged_attention_routed: q must be [total_query, {num_q_heads}, head_dim] with unit inner "
+                         f"stride, got {tuple(q.shape)}")
+    total_q, hq, d = q.shape
+    if num_kv_heads <= 0 or num_q_heads % num_kv_heads:
+        raise ValueError(f"paged_attention_routed: num_q_heads {num_q_heads} not a multiple of {num_kv_heads}")
+    if k_cache.dim() != 4 or k_cache.shape[1] != BLOCK_SIZE or tuple(k_cache.shape[2:]) != (num_kv_heads, d):
+        raise ValueError(f"paged_attention_routed: k_cache must be [num_blocks, {BLOCK_SIZE}, {num_kv_heads}, {d}]")
+    if v_cache.shape != k_cache.shape or not (k_cache.is_contiguous() and v_cache.is_contiguous()):
+        raise ValueError("paged_attention_routed: k_cache and v_cache must be contiguous and of equal shape")
+    if not (q.dtype == k_cache.dtype == v_cache.dtype):
+        raise ValueError("paged_attention_routed: dtype mismatch")
+    for name, t in (("block_table", block_table), ("q_lens", q_lens), ("k_lens", k_lens), ("q_starts", q_starts),
+                    ("q_pos_offsets", q_pos_offsets)):
+        if t.dtype != torch.int32:
+            raise ValueError(f"paged_attention_routed: {name} must be int32")
+    rows = q_lens.numel()
+    if not (k_lens.numel() == q_starts.numel() == q_pos_offsets.numel() == rows):
+        raise ValueError("paged_attention_routed: per-row arrays differ in length")
+    if block_table.dim() != 2 or block_table.shape[0] != rows:
+        raise ValueError(f"paged_attention_routed: block_table must be [{rows}, max_blocks]")
+    if block_table.stride(1) != 1:
+        block_table = block_table.contiguous()
+    q_lens, k_lens, q_starts, q_pos_offsets = (t.contiguous() for t in (q_lens, k_lens, q_starts, q_pos_offsets))
+    if out is None:
+        out = torch.empty_like(q)
+    if lse is None:
+        lse = torch.empty((total_q, num_q_heads), dtype=torch.float32, device=dev)
+    max_blocks = block_table.shape[1]
+    if rows == 0 or total_q == 0:
+        return out, lse
+    if max_blocks == 0:
+        out.fill_(float("nan"))  # every row has k_len 0: O = NaN, LSE = -inf (reference semantics)
+        lse.fill_(float("-inf"))
+        return out, lse
+    nbytes = int(lib().seb_paged_attention_workspace_size(rows, total_q, num_q_heads, num_kv_heads, d, max_blocks))
+    ws = workspace(dev, nbytes)
+    st = lib().seb_paged_attention(
+        q.data_ptr(), q.stride(0), q.stride(1), k_cache.data_ptr(), v_cache.data_ptr(), k_cache.shape[0],
+        block_table.data_ptr(), block_table.stride(0), max_blocks, q_lens.data_ptr(), k_lens.data_ptr(),
+        q_starts.data_ptr(), q_pos_offsets.data_ptr(), rows, total_q, num_q_heads, num_kv_heads, d, dtype_code(q),
+        float(scale), 1 if is_causal else 0, out.data_ptr(), out.stride(0), out.stride(1), lse.data_ptr(),
+        lse.stride(0), ws.data_ptr(), ws.numel(), err_word(dev).data_ptr(), _stream(dev))
+    check("seb_paged_attention", st)
+    LAUNCHES[0] += 3 if (total_q > rows and prefill_supported(q, num_q_heads, num_kv_heads)) else 1
+    _after(dev)
+    return out, lse
+
+
 # -------------------------------------------------------------- paged prefill
 PREFILL_HEAD_DIMS = (64, 128)
 PREFILL_GROUPS = (1, 2, 4, 8, 16)

@@ -72,16 +72,19 @@ class PeerAllReduceNorm:
         every = bytes(every.cpu().tolist())
         self._imported = []
         bases = []
-        for q in range(self.world):
-            if q == self.rank:
-                bases.append(own)
-                continue
-            h = (ctypes.c_uint8 * SEB_PEER_HANDLE_BYTES).from_buffer_copy(
-                every[q * SEB_PEER_HANDLE_BYTES:(q + 1) * SEB_PEER_HANDLE_BYTES])
-            p = ctypes.c_void_p()
-            check("seb_peer_import", lib().seb_peer_import(h, ctypes.byref(p)))
-            self._imported.append(p.value)
-            bases.append(p.value)
+        # CUDA IPC maps a peer's region into the CURRENT device's context: make
+        # it this rank's device whatever the caller's current device is.
+        with torch.cuda.device(self.device):
+            for q in range(self.world):
+                if q == self.rank:
+                    bases.append(own)
+                    continue
+                h = (ctypes.c_uint8 * SEB_PEER_HANDLE_BYTES).from_buffer_copy(
+                    every[q * SEB_PEER_HANDLE_BYTES:(q + 1) * SEB_PEER_HANDLE_BYTES])
+                p = ctypes.c_void_p()
+                check("seb_peer_import", lib().seb_peer_import(h, ctypes.byref(p)))
+                self._imported.append(p.value)
+                bases.append(p.value)
         self._owned = [own]
         self._bind(bases, local_ranks=[self.rank])
         dist.barrier(group=group)
@@ -166,8 +169,9 @@ class PeerAllReduceNorm:
             import torch.distributed as dist
 
             dist.barrier(group=self.group)  # no peer reads or writes this rank's region any more
-            for p in self._imported:
-                check("seb_peer_close", lib().seb_peer_close(p))
+            with torch.cuda.device(self.device):  # the mappings live in this device's context
+                for p in self._imported:
+                    check("seb_peer_close", lib().seb_peer_close(p))
             dist.barrier(group=self.group)  # every peer closed its mapping of this rank's region
         with torch.cuda.device(self.device):
             for p in self._owned:

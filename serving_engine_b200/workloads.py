@@ -89,12 +89,23 @@ def _fill(shape, dtype, gen: torch.Generator, fill: str, seed: int) -> torch.Ten
     return out
 
 
+def decode_k_lens(batch: int, k_min: int, k_max: int, seed: int) -> list[int]:
+    """The k_len draw of decode_batch(batch, k_min, k_max, ..., seed): U[k_min, k_max]."""
+    gen = torch.Generator().manual_seed(seed)
+    return torch.randint(k_min, k_max + 1, (batch,), generator=gen).tolist()
+
+
 def decode_batch(batch: int, k_min: int, k_max: int, num_q_heads: int, num_kv_heads: int, head_dim: int,
                  dtype: torch.dtype, seed: int, num_blocks: int | None = None, pool_factor: float = 1.25,
-                 fill: str = "cpu") -> PagedBatch:
-    """Decode batch: one query per sequence at its last position, k_len ~ U[k_min, k_max]."""
+                 fill: str = "cpu", k_lens: list[int] | None = None) -> PagedBatch:
+    """Decode batch: one query per sequence at its last position, k_len ~ U[k_min, k_max]
+    (or the given per-sequence k_lens; tables, q and the pool still come from `seed`)."""
     gen = torch.Generator().manual_seed(seed)
-    k_lens = torch.randint(k_min, k_max + 1, (batch,), generator=gen).tolist()
+    drawn = torch.randint(k_min, k_max + 1, (batch,), generator=gen).tolist()
+    if k_lens is None:
+        k_lens = drawn
+    elif len(k_lens) != batch:
+        raise ValueError(f"k_lens has {len(k_lens)} entries for a batch of {batch}")
     need = [math.ceil(k / BLOCK_SIZE) for k in k_lens]
     if num_blocks is None:
         num_blocks = max(math.ceil(pool_factor * sum(k_lens) / BLOCK_SIZE), sum(need))

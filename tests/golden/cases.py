@@ -73,3 +73,29 @@ def e2e_prompts():
     gen = torch.Generator().manual_seed(31)
     lens = [20, 37, 5, 64]
     return [torch.randint(0, 1000, (n,), generator=gen).tolist() for n in lens], 12
+
+
+def e2e_config4_workload() -> dict:
+    """The end-to-end parity run on the config-4 model shape (16 layers, hidden
+    2048, 32/8 heads, head_dim 64, FFN 8192, vocab 32000), reduced so the
+    reference engine can run it on the CPU in fp32: 12 requests, token ids
+    U[0, 32000), prompt lengths lognormal around 64 (the workload generator's
+    cv = 1 spread) clipped to [20, 200], 16 greedy tokens each. Requests 3, 9
+    and 11 start with request 0's first 48 tokens (three full blocks): 9 and 11
+    arrive after request 0's blocks are registered and hit the prefix cache.
+    8 requests arrive at step 0 and one each at steps 6, 10, 18 and 26. A
+    96-token budget forces chunked prefill and mixed steps; a 20-block pool
+    forces a preemption with recompute."""
+    import math
+
+    import numpy as np
+
+    rng = np.random.default_rng(0)
+    sigma = math.sqrt(math.log(2.0))
+    lens = np.clip(np.round(np.exp(rng.normal(math.log(64.0), sigma, size=12))), 20, 200).astype(int)
+    prompts = [rng.integers(0, 32000, size=int(k)).tolist() for k in lens]
+    for j in (3, 9, 11):
+        prompts[j] = prompts[0][:48] + prompts[j][:max(len(prompts[j]) - 48, 5)]
+    return {"prompts": prompts, "max_new": 16, "num_gpu_blocks": 20, "max_num_batched_tokens": 96,
+            "max_num_seqs": None, "min_chunk_size": None,
+            "arrivals": {0: list(range(8)), 6: [8], 10: [9], 18: [10], 26: [11]}, "model": "config4", "seed": 0}

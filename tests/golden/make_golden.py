@@ -18,7 +18,13 @@ oracle (transformers' eager_paged_attention_forward) and records:
 * the pool after _PagedKVCache.write (index_copy_) of strided K/V views;
 * build_paged_batch_metadata outputs and per-token write slots
   (ModelRunner._flat_slot) over a scripted run of the reference
-  Scheduler/BlockManager with chunked prefill, decode and prefix sharing.
+  Scheduler/BlockManager with chunked prefill, decode and prefix sharing;
+* greedy tokens of the reference engine itself (fp32, CPU) on a tiny random
+  Llama, and on the config-4 model shape with a reduced workload whose
+  schedule has chunked prefill, prefix-cache hits and a preemption: its
+  per-step schedule and the top-5 logits behind every sampled token too.
+
+``--only PART`` regenerates just that part and keeps the other fixtures.
 
 Inputs are regenerated in the tests from the same seeds
 (serving_engine_b200.workloads); their sha256 is stored to prove it.
@@ -219,17 +225,112 @@ def e2e_trace(meta: dict) -> None:
                              "max_num_batched_tokens": 32, "num_gpu_blocks": 64, "model": "tiny", "seed": 0}
 
 
+def e2e_config4_trace(out: dict, meta: dict) -> None:
+    """The reference engine (LLMEngine + Scheduler + BlockManager +
+    ModelRunner.forward, eager paged attention, fp32, CPU) on the config-4 model
+    shape with the reduced workload of cases.e2e_config4_workload: requests
+    arrive at their listed steps, and each step is engine.step() (engine.py:92-116)
+    written out, as the reference's own scripts/diagnose_triton_kernel_divergence.py
+    does, so the logits behind every sampled token can be kept. Records the
+    schedule of every step (rows: request index, phase, chunk, computed tokens,
+    block table; preempted request indices), the greedy tokens, and per sampled
+    token its top-5 token ids and logits."""
+    from serving_engine.block import BLOCK_SIZE
+    from serving_engine.block_manager import BlockManager
+    from serving_engine.engine import LLMEngine
+    from serving_engine.model_runner import ModelRunner
+    from serving_engine.request import RequestPhase
+    from serving_engine.scheduler import Scheduler
+
+    from serving_engine_b200.e2e import random_llama
+    from tests.golden.cases import e2e_config4_workload
+
+    w = e2e_config4_workload()
+    model = random_llama(w["model"], seed=w["seed"])
+    cfg = model.config
+    nb = w["num_gpu_blocks"]
+    runner = object.__new__(ModelRunner)
+    runner.device = "cpu"
+    runner.dtype = torch.float32
+    runner.attn_implementation = "paged|eager"
+    runner.model = model
+    runner.model.set_attn_implementation("paged|eager")
+    runner.block_size = BLOCK_SIZE
+    runner.num_gpu_blocks = nb
+    runner.tokenizer = None
+    runner.kv_cache = torch.zeros(cfg.num_hidden_layers, 2, nb, BLOCK_SIZE, cfg.num_key_value_heads, cfg.head_dim)
+    engine = object.__new__(LLMEngine)
+    engine.model_runner = runner
+    engine.block_manager = BlockManager(nb, BLOCK_SIZE)
+    engine.scheduler = Scheduler(engine.block_manager, max_num_batched_tokens=w["max_num_batched_tokens"],
+                                 max_num_seqs=w["max_num_seqs"], min_chunk_size=w["min_chunk_size"])
+    engine.requests = {}
+    index = {}
+    trace, sampled, top_ids, top_vals = [], [], [], []
+    step = 0
+    last_arrival = max(w["arrivals"])
+    while True:
+        for i in w["arrivals"].get(step, []):
+            rid = engine.add_request(prompt_token_ids=w["prompts"][i], max_new_tokens=w["max_new"], ignore_eos=True)
+            index[rid] = i
+        if not engine.scheduler.has_unfinished_requests() and step > last_arrival:
+            break
+        so = engine.scheduler.schedule()
+        step += 1
+        trace.append({"rows": [[index[r.request_id], "P" if r.phase == RequestPhase.NEEDS_PREFILL else "D",
+                                so.prefill_chunk_sizes.get(r.request_id, 0), r.num_computed_tokens,
+                                list(r.block_table)] for r in so.scheduled_requests],
+                      "preempted": [index[r.request_id] for r in so.preempted_requests]})
+        if not so.scheduled_requests:
+            continue
+        logits = engine.model_runner.forward(so)
+        next_tokens = logits.argmax(dim=-1)
+        top = torch.topk(logits.float(), 5, dim=-1)
+        for j, (req, tok) in enumerate(zip(so.scheduled_requests, next_tokens)):
+            if req.phase == RequestPhase.NEEDS_DECODE or req.request_id in so.prefill_final_chunk:
+                sampled.append([index[req.request_id], req.output_len])
+                top_ids.append(top.indices[j].tolist())
+                top_vals.append(top.values[j].tolist())
+                req.output_token_ids.append(tok.item())
+        engine.scheduler.update_after_step(so)
+        print("e2e config4 step", step, flush=True)
+    outputs = [None] * len(w["prompts"])
+    for rid, i in index.items():
+        outputs[i] = engine.requests[rid].output_token_ids
+    vals = np.asarray(top_vals, dtype=np.float32)
+    meta["e2e_config4_fp32"] = {"outputs": outputs, "trace": trace, "steps": step, "sampled": sampled,
+                                "min_top1_margin": float((vals[:, 0] - vals[:, 1]).min()),
+                                "preemptions": sum(len(t["preempted"]) for t in trace)}
+    out["e2e_config4_fp32__top5_ids"] = np.asarray(top_ids, dtype=np.int32)
+    out["e2e_config4_fp32__top5_logits"] = vals
+
+
+PARTS = ("attention", "kv_append", "scheduler_trace", "e2e_tiny", "e2e_config4")
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default=os.environ.get("SEB_REFERENCE", "/root/reference"))
+    ap.add_argument("--only", choices=PARTS, action="append",
+                    help="regenerate only these parts and keep the rest of the existing fixtures")
     args = ap.parse_args()
     sys.path.insert(0, args.reference)
     torch.set_num_threads(max(1, os.cpu_count() or 1))
+    parts = set(args.only or PARTS)
     arrays, meta = {}, {}
-    attention_cases(arrays, meta)
-    kv_append_case(arrays, meta)
-    scheduler_trace(meta)
-    e2e_trace(meta)
+    if args.only:
+        arrays = dict(np.load(HERE / "golden.npz"))
+        meta = json.loads((HERE / "golden.json").read_text())
+    if "attention" in parts:
+        attention_cases(arrays, meta)
+    if "kv_append" in parts:
+        kv_append_case(arrays, meta)
+    if "scheduler_trace" in parts:
+        scheduler_trace(meta)
+    if "e2e_tiny" in parts:
+        e2e_trace(meta)
+    if "e2e_config4" in parts:
+        e2e_config4_trace(arrays, meta)
     import transformers
     meta["_generated_with"] = {"torch": torch.__version__, "transformers": transformers.__version__,
                                "numpy": np.__version__}

@@ -4,22 +4,33 @@ Some callers cannot give the library a workspace: their device memory is
 owned by another allocator (the engine sizes its KV pool to most of the free
 memory at start-up), or they bind the C ABI from a language with no access to
 the framework's allocator. For them the library keeps its split-K scratch in a
-fixed device array of its own. These tests call that entry point through the
-C ABI and check, on two different calls in a row (the second one finds the
-first one's leftovers in the shared scratch), that it returns what the
-workspace-taking seb_paged_decode returns, within the tolerances the other
-decode tests use. The file runs last so a failure here cannot hide others.
+fixed device array of its own.
+
+These tests call that entry point through the C ABI on two different calls in
+a row (the second one finds the first one's leftovers in the shared scratch)
+and check that
+  * it returns exactly what the workspace-taking seb_paged_decode returns (the
+    same kernel with the same split length and a fixed merge order, so O and
+    LSE must be bitwise equal),
+  * sampled rows agree with the CPU oracle within the decode tolerance
+    (tests/tolerance.py), so a fault shared by both entry points is caught too,
+  * the device's free memory does not change across its calls: it allocates
+    nothing.
+The file runs last so a failure here cannot hide others.
 """
 import numpy as np
 import pytest
 import torch
 
+from oracle.paged_attention import decode_rows
 from serving_engine_b200 import _lib, workloads
 from serving_engine_b200.build import build
 from serving_engine_b200.ops import decode_workspace_bytes, dtype_code
 from serving_engine_b200.paged_attention import metadata_from_lists
+from tests.tolerance import LSE_TOL, check_out
 
 pytestmark = pytest.mark.gpu
+SAMPLED_ROWS = (0, 5, 11)
 
 
 def _common_args(b, md, q, out, lse):
@@ -31,44 +42,64 @@ def _common_args(b, md, q, out, lse):
             out.data_ptr(), out.stride(0), out.stride(1), lse.data_ptr(), lse.stride(0)]
 
 
-def _run_both(lib, b):
-    dev = torch.device("cuda", 0)
-    md = metadata_from_lists(b.q_lens, b.k_lens, b.q_starts, b.q_pos_offsets, b.block_tables, dev)
-    q = b.q.to(dev)
-    err = torch.zeros(1, dtype=torch.int32, device=dev)
-    stream = torch.cuda.current_stream(dev).cuda_stream
-    ws_bytes = decode_workspace_bytes(q.shape[0], b.num_q_heads, b.num_kv_heads, b.head_dim,
-                                      md["block_table"].shape[1])
-    assert 0 < ws_bytes <= _lib.NOALLOC_SCRATCH_BYTES  # split-K is in play, so the scratch is used
-    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
-    o_ws, l_ws = torch.empty_like(q), torch.empty(q.shape[0], b.num_q_heads, dtype=torch.float32, device=dev)
-    o_na, l_na = torch.empty_like(q), torch.empty_like(l_ws)
-    st = lib.seb_paged_decode(*_common_args(b, md, q, o_ws, l_ws), ws.data_ptr(), ws.numel(), err.data_ptr(),
-                              stream)
-    assert st == 0, lib.seb_last_error()
-    st = lib.seb_paged_decode_noalloc(*_common_args(b, md, q, o_na, l_na), err.data_ptr(), stream)
-    assert st == 0, lib.seb_last_error()
-    torch.cuda.synchronize(dev)
-    assert int(err.item()) == 0
-    return o_ws.float().cpu().numpy(), l_ws.cpu().numpy(), o_na.float().cpu().numpy(), l_na.cpu().numpy()
+class _Case:
+    """Device inputs and preallocated outputs of one decode batch."""
 
+    def __init__(self, b):
+        dev = torch.device("cuda", 0)
+        self.b = b
+        self.md = metadata_from_lists(b.q_lens, b.k_lens, b.q_starts, b.q_pos_offsets, b.block_tables, dev)
+        self.q = b.q.to(dev)
+        self.err = torch.zeros(1, dtype=torch.int32, device=dev)
+        ws_bytes = decode_workspace_bytes(self.q.shape[0], b.num_q_heads, b.num_kv_heads, b.head_dim,
+                                          self.md["block_table"].shape[1])
+        # split-K is in play, so the scratch is used, and it fits the built-in array
+        assert 0 < ws_bytes <= _lib.NOALLOC_SCRATCH_BYTES
+        self.ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
+        self.o_ws, self.l_ws = torch.empty_like(self.q), torch.empty(self.q.shape[0], b.num_q_heads,
+                                                                      dtype=torch.float32, device=dev)
+        self.o_na, self.l_na = torch.empty_like(self.q), torch.empty_like(self.l_ws)
+        self.stream = torch.cuda.current_stream(dev).cuda_stream
 
-def _assert_within_decode_tolerance(o, o_ref, lse, lse_ref):
-    """bf16: 2e-3 plus half a bf16 ulp on O, 1e-3 on LSE (the other decode tests' bar)."""
-    tol = 2e-3 + np.exp2(np.floor(np.log2(np.maximum(np.abs(o_ref), 1e-30))) - 8)
-    assert (np.abs(o - o_ref) <= tol).all()
-    np.testing.assert_allclose(lse, lse_ref, atol=1e-3, rtol=0)
+    def run_workspace(self, lib):
+        st = lib.seb_paged_decode(*_common_args(self.b, self.md, self.q, self.o_ws, self.l_ws), self.ws.data_ptr(),
+                                  self.ws.numel(), self.err.data_ptr(), self.stream)
+        assert st == 0, lib.seb_last_error()
+
+    def run_noalloc(self, lib):
+        st = lib.seb_paged_decode_noalloc(*_common_args(self.b, self.md, self.q, self.o_na, self.l_na),
+                                          self.err.data_ptr(), self.stream)
+        assert st == 0, lib.seb_last_error()
 
 
 def test_noalloc_matches_workspace_entry_point_two_calls_in_a_row():
     build()
     lib = _lib.lib()
-    first = workloads.decode_batch(16, 1024, 4096, 32, 8, 128, torch.bfloat16, seed=71, fill="cuda")
-    second = workloads.decode_batch(24, 300, 3000, 16, 4, 128, torch.bfloat16, seed=72, fill="cuda")
-    for b in (first, second):
-        o_ws, l_ws, o_na, l_na = _run_both(lib, b)
-        assert np.isfinite(o_na).all() and np.isfinite(l_na).all()
-        _assert_within_decode_tolerance(o_na, o_ws, l_na, l_ws)
+    cases = [_Case(workloads.decode_batch(16, 1024, 4096, 32, 8, 128, torch.bfloat16, seed=71, fill="cuda")),
+             _Case(workloads.decode_batch(24, 300, 3000, 16, 4, 128, torch.bfloat16, seed=72, fill="cuda"))]
+    for c in cases:
+        c.run_workspace(lib)
+    # The first call on the device looks the scratch up (the module may load
+    # then); from there on no call may change the device's free memory.
+    cases[0].run_noalloc(lib)
+    torch.cuda.synchronize()
+    free_before, _ = torch.cuda.mem_get_info()
+    for c in cases:  # the second call finds the first one's leftovers in the scratch
+        c.run_noalloc(lib)
+    torch.cuda.synchronize()
+    free_after, _ = torch.cuda.mem_get_info()
+    assert free_after == free_before, f"free device memory changed by {free_before - free_after} bytes"
+    for c in cases:
+        assert int(c.err.item()) == 0
+        assert torch.equal(c.o_na.view(torch.int16), c.o_ws.view(torch.int16)), "O differs from seb_paged_decode"
+        assert torch.equal(c.l_na, c.l_ws), "LSE differs from seb_paged_decode"
+        b = c.b
+        ref = decode_rows(b.q, b.k_cache, b.v_cache, b.block_tables, b.k_lens, b.scale, SAMPLED_ROWS)
+        for r in SAMPLED_ROWS:
+            o_ref, lse_ref = ref[r]
+            ok, msg = check_out(c.o_na[r].float().cpu().numpy(), o_ref, torch.bfloat16)
+            assert ok, f"row {r}: {msg}"
+            np.testing.assert_allclose(c.l_na[r].cpu().numpy(), lse_ref, atol=LSE_TOL["bf16"], rtol=0)
 
 
 def test_noalloc_rejects_a_call_beyond_its_scratch():
@@ -82,4 +113,5 @@ def test_noalloc_rejects_a_call_beyond_its_scratch():
                                       items, items, None, None, items, hq, hkv, d, _lib.SEB_BF16, 0.1, 1, 0,
                                       None, 0, 0, None, 0, None, None)
     assert st == _lib.SEB_EWORKSPACE
-    assert b"built-in scratch" in lib.seb_last_error()
+    msg = lib.seb_last_error()
+    assert b"built-in scratch" in msg and b"capped at 32" in msg
