@@ -56,6 +56,10 @@ def parse_args():
                     help="decode: config 2 (the headline line); prefill: config 3; e2e: config 4; "
                          "tp: config 5 (tensor-parallel decode)")
     ap.add_argument("--tp-batch", type=int, default=256)
+    ap.add_argument("--tp-steps", type=int, default=20, help="timed decode steps of the config-5 workload")
+    ap.add_argument("--no-e2e-decode", action="store_true",
+                    help="decode line: skip the end-to-end decode tok/s sub-record (config 4 / config 5)")
+    ap.add_argument("--no-prefill", action="store_true", help="decode line: skip the config-3 prefill sub-record")
     ap.add_argument("--tp-context", type=int, default=4096)
     ap.add_argument("--no-graph", action="store_true", help="tp / e2e: run decode steps eagerly")
     ap.add_argument("--tp-allreduce", default="peer", choices=["peer", "nccl"],
@@ -305,7 +309,8 @@ def run_ours(args, rank, world, device, dist):
         "traffic_source": "profiles/traffic.json (one ncu capture of this per-GPU workload)",
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        result["cpu_baseline"] = cpu_baseline(b, budget_s=12.0)
+        port = cpu_baseline(b, budget_s=12.0)
+        result["cpu_baseline"] = dict(port, port=dict(port), stock_eager=stock_eager_baseline())
     return result
 
 
@@ -422,6 +427,84 @@ def cpu_baseline(b, budget_s: float) -> dict:
     return {"value": round(gbs, 4), "unit": "GB/s", "cores": cores, "kind": "port",
             "sample": f"{len(used)} of {len(rows_all)} config-2 sequences ({done_bytes / 1e9:.2f} GB bf16-equivalent KV, "
                       f"{done_t:.1f} s), oracle/paged_attention.py in numpy float32 (multithreaded BLAS)"}
+
+
+class _WriteThenGather:
+    """The cache contract the stock eager op calls (cache.update), restated from
+    the reference's _PagedKVCache.update (serving_engine/model_runner.py:21-40):
+    index_copy_ of the step's new K/V rows into the flat pool at write_index,
+    then index_select of read_index."""
+
+    def __init__(self, kv: torch.Tensor):
+        self.kv = kv  # [layers, 2, num_blocks, 16, kv heads, head_dim]
+
+    def update(self, key_states, value_states, layer_idx, read_index, write_index):
+        h, d = self.kv.shape[-2:]
+        k_flat = self.kv[layer_idx, 0].view(-1, h, d)
+        v_flat = self.kv[layer_idx, 1].view(-1, h, d)
+        k_flat.index_copy_(0, write_index, key_states.transpose(1, 2).squeeze(0))
+        v_flat.index_copy_(0, write_index, value_states.transpose(1, 2).squeeze(0))
+        return torch.index_select(k_flat, 0, read_index), torch.index_select(v_flat, 0, read_index)
+
+
+def stock_eager_baseline(budget_s: float = 6.0, seed: int = 0) -> dict:
+    """The reference's stock CPU attention path at config 1 (fp32, 8 decode rows,
+    k_len U[1, 512], 12/12 heads, head_dim 64): transformers'
+    eager_paged_attention_forward (the op behind "paged|eager") with the
+    write-then-gather cache above and the additive mask built as
+    ModelRunner.forward builds it (model_runner.py:185-207: same request and key
+    position <= query position, else finfo.min), timed per call (one layer) on
+    all host threads for about budget_s seconds."""
+    import types
+
+    from transformers.integrations.eager_paged import eager_paged_attention_forward
+
+    from serving_engine_b200 import workloads
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    b = workloads.config1(seed=seed)
+    hkv, d = b.num_kv_heads, b.head_dim
+    kv = torch.stack([b.k_cache, b.v_cache]).unsqueeze(0).clone()
+    write, q_group, q_pos, read, k_pos, k_group = [], [], [], [], [], []
+    for r, bt in enumerate(b.block_tables):
+        p = b.q_pos_offsets[r]
+        write.append(bt[p // 16] * 16 + p % 16)
+        q_group.append(r)
+        q_pos.append(p)
+        for j in range(b.k_lens[r]):
+            read.append(bt[j // 16] * 16 + j % 16)
+            k_pos.append(j)
+            k_group.append(r)
+    write_t, read_t = torch.tensor(write), torch.tensor(read)
+    allowed = (torch.tensor(q_group)[:, None] == torch.tensor(k_group)[None, :]) & (
+        torch.tensor(k_pos)[None, :] <= torch.tensor(q_pos)[:, None])
+    mask = torch.zeros(len(q_pos), len(read), dtype=torch.float32)
+    mask.masked_fill_(~allowed, torch.finfo(torch.float32).min)
+    mask = mask[None, None]
+    flat_k = kv[0, 0].view(-1, hkv, d)
+    flat_v = kv[0, 1].view(-1, hkv, d)
+    key = flat_k[write_t].transpose(0, 1).unsqueeze(0).clone()
+    value = flat_v[write_t].transpose(0, 1).unsqueeze(0).clone()
+    query = b.q.transpose(0, 1).unsqueeze(0)
+    module = types.SimpleNamespace(layer_idx=0, num_key_value_groups=b.num_q_heads // hkv)
+    cache = _WriteThenGather(kv)
+
+    def call():
+        eager_paged_attention_forward(module, query, key, value, mask, b.scale, cache=cache, read_index=read_t,
+                                      write_index=write_t)
+
+    call()
+    n, t0 = 0, time.perf_counter()
+    while time.perf_counter() - t0 < budget_s or n < 3:
+        call()
+        n += 1
+    dt = (time.perf_counter() - t0) / n
+    nbytes = sum(b.k_lens) * hkv * d * 2 * 4
+    return {"value": round(nbytes / dt / 1e9, 4), "unit": "GB/s", "ms_per_call": round(dt * 1e3, 3),
+            "cores": torch.get_num_threads(), "kind": "reference",
+            "sample": f"config 1 (fp32, 8 rows, sum k_len {sum(b.k_lens)}), {n} timed calls of "
+                      "transformers eager_paged_attention_forward with the reference's mask and write-then-gather "
+                      "cache update (one layer per call; index building outside the timed call)"}
 
 
 def _row_sample(b, row, kv_heads):
@@ -588,11 +671,20 @@ def run_e2e_workload(args, device):
     """Config 4: random-init 16-layer Llama (hidden 2048, 32/8 heads, FFN 8192,
     vocab 32000), bf16, 256 requests arriving at t=0 with lognormal prompts
     (median 512, clipped to [32, 4096]) and 128 greedy tokens each, served with
-    continuous batching through the registered "paged|b200" attention."""
-    from serving_engine_b200 import ops
-    from serving_engine_b200.e2e import E2EEngine, config4_requests, random_llama
+    continuous batching through the registered "paged|b200" attention.
 
-    model = random_llama("config4", seed=args.seed, dtype=torch.bfloat16, device=device)
+    Decode-only steps (CUDA graphs) are reported with their HBM bytes: the
+    weights read once per step plus every row's K/V (32 KiB per token) read by
+    the attention of all 16 layers, against MEASURED_PEAKS.json hbm_gbs."""
+    from serving_engine_b200 import ops
+    from serving_engine_b200.e2e import E2EEngine, config4_requests, llama_config, random_llama
+
+    # initialised on the device (seconds instead of a minute); the parity tests
+    # use the CPU initialisation instead
+    model = random_llama("config4", seed=args.seed, dtype=torch.bfloat16, device=device, init_on_device=True)
+    cfg = llama_config("config4")
+    weight_bytes = sum(p.numel() * p.element_size() for p in model.parameters())
+    kv_bytes_per_token = cfg.num_hidden_layers * 2 * cfg.num_key_value_heads * cfg.head_dim * 2
     prompts = config4_requests(seed=args.seed)
     max_new = 128
     total_tokens = sum(len(p) + max_new for p in prompts)
@@ -606,7 +698,7 @@ def run_e2e_workload(args, device):
     torch.cuda.synchronize(device)
     graphs = not args.no_graph
     eng = E2EEngine(model, num_blocks=num_blocks, max_num_batched_tokens=args.e2e_budget, max_num_seqs=256,
-                    use_graphs=graphs, max_context=4096 + max_new)
+                    use_graphs=graphs, max_context=4096 + max_new, record_trace=False)
     if graphs:
         eng.capture_graphs()
     for p in prompts:
@@ -621,10 +713,12 @@ def run_e2e_workload(args, device):
     dec = [st for st in eng.stats if st.kind == "decode"]
     dec_tok = sum(st.new_tokens for st in dec)
     dec_s = sum(st.seconds for st in dec)
-    pre = [st for st in eng.stats if st.kind != "decode"]
+    dec_bytes = sum(weight_bytes + st.kv_tokens * kv_bytes_per_token for st in dec)
+    pre = [st for st in eng.stats if st.kind not in ("decode", "idle")]
     pre_tok = sum(st.tokens for st in pre)
     pre_s = sum(st.seconds for st in pre)
-    return {
+    hbm = peaks()[0]
+    res = {
         "metric": "end-to-end decode tokens/sec (config 4)", "value": round(gen / wall, 1), "unit": "tokens/s",
         "n_gpus": 1, "steps": len(eng.stats), "warmup": 1, "ms_per_step": round(wall / len(eng.stats) * 1e3, 3),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
@@ -636,11 +730,18 @@ def run_e2e_workload(args, device):
                    "cuda_graph_decode": graphs},
         "wall_s": round(wall, 3),
         "decode_only": {"tokens_per_s": round(dec_tok / dec_s, 1) if dec_s else None, "steps": len(dec),
-                        "ms_per_step": round(dec_s / max(len(dec), 1) * 1e3, 3)},
+                        "ms_per_step": round(dec_s / max(len(dec), 1) * 1e3, 3),
+                        "hbm_bytes_per_step": int(dec_bytes / max(len(dec), 1)),
+                        "hbm_gbs": round(dec_bytes / dec_s / 1e9, 1) if dec_s else None,
+                        "hbm_frac": round(dec_bytes / dec_s / 1e9 / hbm, 4) if dec_s else None,
+                        "timing": "host wall clock per step (graph replay and the token read-back included)"},
         "prefill_steps": {"steps": len(pre), "seconds": round(pre_s, 3), "query_tokens": pre_tok,
                           "query_tokens_per_s": round(pre_tok / pre_s, 1) if pre_s else None},
         "gpu_launches": ops.LAUNCHES[0] - launches0,
     }
+    del eng, model
+    torch.cuda.empty_cache()
+    return res
 
 
 # ---------------------------------------------------- config 5 tensor-parallel decode
@@ -648,12 +749,14 @@ def run_tp_workload(args, rank, world, device, dist):
     """Config 5: random-init Llama-3-8B shape (32 layers, 4096, 32/8 heads, D=128,
     FFN 14336, vocab 128256), bf16, decode batch 256 at 4096 context over a
     synthetic pre-filled KV pool; weights and pool sharded by kv head over the
-    ranks, NCCL all-reduce after o_proj and down_proj (64 per step)."""
+    ranks, an all-reduce after o_proj and down_proj (64 per step) fused with the
+    residual add + RMSNorm over peer memory (or NCCL, --tp-allreduce nccl)."""
     from serving_engine_b200 import ops
     from serving_engine_b200.tp_decode import LLAMA3_8B, TPLlamaDecoder
 
+    group = dist.group.WORLD if dist is not None else None
     dec = TPLlamaDecoder(LLAMA3_8B, rank, world, device, batch=args.tp_batch, context=args.tp_context,
-                         seed=args.seed, allreduce=args.tp_allreduce)
+                         seed=args.seed, group=group, allreduce=args.tp_allreduce)
     graph = not args.no_graph
     if graph:
         dec.capture(warmup=2)
@@ -665,33 +768,114 @@ def run_tp_workload(args, rank, world, device, dist):
     stream = torch.cuda.current_stream(device)
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     launches0 = ops.LAUNCHES[0]
+    steps = args.tp_steps
     ev0.record(stream)
-    for _ in range(args.steps):
+    for _ in range(steps):
         dec.step()
     ev1.record(stream)
     torch.cuda.synchronize(device)
     ops.check_device_errors(device)
-    ms = max_over_ranks(dist, ev0.elapsed_time(ev1), device) / args.steps
-    kv_bytes = dec.kv.numel() * 2 // LLAMA3_8B.layers * LLAMA3_8B.layers  # whole pool shard read per step
+    per_rank_ms = gather_over_ranks(dist, ev0.elapsed_time(ev1) / steps, device)
+    ms = max(per_rank_ms)
+    kv_bytes = dec.kv.numel() * dec.kv.element_size()  # the whole pool shard is read once per step
     weight_bytes = sum(t.numel() * 2 for w in dec.layers for t in w.values()) + dec.lm_head.numel() * 2
     per_gpu_bytes = kv_bytes + weight_bytes
+    allreduce = dec.allreduce if world > 1 else None
     dec.release()
+    del dec
+    torch.cuda.empty_cache()
+    hbm = peaks()[0]
     res = {
         "metric": "tensor-parallel decode tokens/sec (config 5)", "value": round(args.tp_batch / (ms * 1e-3), 1),
-        "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
+        "unit": "tokens/s", "n_gpus": world, "steps": steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (random-init weights, random pre-filled KV)",
         "config": {"workload": "config 5: Llama-3-8B shape, decode batch 256 at 4096 context",
                    "batch": args.tp_batch, "context": args.tp_context, "parallelism": f"tp{world} (kv-head shard)",
                    "cuda_graph": graph, "all_reduces_per_step": 2 * LLAMA3_8B.layers if world > 1 else 0,
-                   "all_reduce": dec.allreduce if world > 1 else None},
+                   "all_reduce": allreduce},
+        "per_rank_ms_per_step": {"min": round(min(per_rank_ms), 4), "max": round(ms, 4)},
         "hbm_bytes_per_step_per_gpu": per_gpu_bytes,
         "roofline": {"bound": "hbm", "achieved": round(per_gpu_bytes / (ms * 1e-3) / 1e9, 1), "unit": "GB/s",
-                     "peak": peaks()[0], "frac": round(per_gpu_bytes / (ms * 1e-3) / 1e9 / peaks()[0], 4),
-                     "note": "weights + KV shard read once per step per GPU"},
-        "gpu_launches_per_step": None if graph else (ops.LAUNCHES[0] - launches0) // args.steps,
+                     "peak": hbm, "frac": round(per_gpu_bytes / (ms * 1e-3) / 1e9 / hbm, 4),
+                     "note": "weights + KV shard read once per step per GPU; CUDA events over the timed steps"},
+        "gpu_launches_per_step": None if graph else (ops.LAUNCHES[0] - launches0) // steps,
     }
     return res
+
+
+def tp_parity(args, rank, world, device, dist, batch: int = 8, context: int = 512, steps: int = 4):
+    """TP=world against TP=1 on the config-5 model shape at a small batch,
+    teacher-forced so both see the same tokens at every step.
+
+    Rank 0 first runs the unsharded decoder (the same seeded weights and pool)
+    and an fp32 dense restatement of the same step (TPLlamaDecoder
+    .reference_logits); the fp32 argmax is the next step's token. The tokens go
+    to every rank, which then runs the sharded decoder on them. Rank 0 reports
+    per step the largest logit difference of TP=world against TP=1 and of each
+    against fp32, whether TP=world's greedy tokens equal TP=1's, and every
+    disagreement with the fp32 model's margin between the two tokens: a
+    disagreement is a near-tie when that margin is within the step's logit
+    difference (the reference's own triage rule,
+    scripts/diagnose_triton_kernel_divergence.py:1-18)."""
+    from serving_engine_b200.tp_decode import LLAMA3_8B, TPLlamaDecoder
+
+    group = dist.group.WORLD if dist is not None else None
+    seed = args.seed + 101
+    toks = torch.zeros(steps, batch, dtype=torch.int64, device=device)
+    one = None
+    if rank == 0:
+        ref = TPLlamaDecoder(LLAMA3_8B, 0, 1, device, batch=batch, context=context, seed=seed)
+        one = []
+        tok = torch.zeros(batch, dtype=torch.int64, device=device)
+        for st in range(steps):
+            toks[st] = tok
+            l1 = ref.logits(tok).float()
+            l32 = ref.reference_logits(tok).float()
+            one.append((l1.cpu(), l32.cpu()))
+            tok = l32.argmax(dim=-1)
+        torch.cuda.synchronize(device)
+        del ref
+        torch.cuda.empty_cache()
+    if dist is not None:
+        dist.broadcast(toks, src=0)
+    dec = TPLlamaDecoder(LLAMA3_8B, rank, world, device, batch=batch, context=context, seed=seed,
+                         group=group, allreduce=args.tp_allreduce)
+    sharded = [dec.logits(toks[st]).float().cpu() for st in range(steps)]
+    torch.cuda.synchronize(device)
+    dec.release()
+    del dec
+    torch.cuda.empty_cache()
+    out = None
+    if rank == 0:
+        per_step, mism, equal = [], [], True
+        for st in range(steps):
+            ln, (l1, l32) = sharded[st], one[st]
+            d_n1 = float((ln - l1).abs().max())
+            d_n32 = float((ln - l32).abs().max())
+            d_132 = float((l1 - l32).abs().max())
+            a_n, a_1, a_32 = ln.argmax(-1), l1.argmax(-1), l32.argmax(-1)
+            equal = equal and bool(torch.equal(a_n, a_1))
+            for r in range(batch):
+                if a_n[r] != a_1[r]:
+                    margin = float(l32[r].max() - l32[r, a_n[r]]) if a_n[r] != a_32[r] else float(
+                        l32[r].max() - l32[r, a_1[r]])
+                    mism.append({"step": st, "row": r, "tp_n": int(a_n[r]), "tp_1": int(a_1[r]),
+                                 "fp32": int(a_32[r]), "fp32_margin": round(margin, 5),
+                                 "near_tie": margin <= max(d_n32, d_132)})
+            per_step.append({"tpN_vs_tp1": round(d_n1, 4), "tpN_vs_fp32": round(d_n32, 4),
+                             "tp1_vs_fp32": round(d_132, 4), "logit_absmax": round(float(l32.abs().max()), 3),
+                             "tpN_top1_equals_fp32": int((a_n == a_32).sum()), "tp1_top1_equals_fp32":
+                                 int((a_1 == a_32).sum())})
+        out = {"tp": world, "batch": batch, "context": context, "steps": steps,
+               "max_abs_logit_diff": max(p["tpN_vs_tp1"] for p in per_step), "tokens_equal": equal,
+               "mismatches": mism, "all_mismatches_near_ties": all(m["near_tie"] for m in mism),
+               "per_step": per_step,
+               "how": "config-5 model shape, teacher-forced with the fp32 restatement's greedy tokens; TP=N "
+                      f"({args.tp_allreduce} all-reduce) and TP=1 (bf16 kernels) against each other and fp32"}
+    if dist is not None:
+        dist.barrier()
+    return out
 
 
 def main():
@@ -731,11 +915,33 @@ def main():
             result = run_tp_workload(args, rank, world, device, dist)
         else:
             result = run_ours(args, rank, world, device, dist)
+            torch.cuda.empty_cache()
+            add_sub_records(result, args, rank, world, device, dist)
         if rank == 0:
             print(json.dumps(result), flush=True)
     finally:
         if dist is not None:
             dist.destroy_process_group()
+
+
+def add_sub_records(result, args, rank, world, device, dist):
+    """The metric's second half and the other kernels, in the headline line:
+    ``e2e_decode`` holds end-to-end decode tokens/s -- at 1 GPU config 4 (the
+    serving engine over a 16-layer Llama) and config 5 at TP=1, at N GPUs
+    config 5 at TP=N with a TP=N-against-TP=1 logit check -- and ``prefill``
+    the config-3 chunked-prefill attention TFLOP/s (1 GPU). Every rank takes the
+    same collective steps."""
+    if not args.no_e2e_decode:
+        sub = {}
+        if world == 1:
+            sub["config4"] = run_e2e_workload(args, device)
+            sub["config5"] = run_tp_workload(args, 0, 1, device, None)
+        else:
+            sub["config5"] = run_tp_workload(args, rank, world, device, dist)
+            sub["tp_parity"] = tp_parity(args, rank, world, device, dist)
+        result["e2e_decode"] = sub
+    if world == 1 and not args.no_prefill:
+        result["prefill"] = run_prefill_workload(args, device)
 
 
 if __name__ == "__main__":

@@ -65,6 +65,8 @@ class Seq:
     decoding: bool = False           # phase: prefill until its last chunk ran
     status: str = "waiting"          # waiting | running | preempted | finished
     preemptions: int = 0
+    np_table: np.ndarray | None = None  # int32 copy of `table` for the graph inputs; dropped on release
+    np_copied: int = 0                  # entries of `table` copied into np_table
 
     @property
     def total_len(self) -> int:
@@ -151,6 +153,7 @@ class BlockPool:
                     del self.by_hash[h]
                     self.block_hash[bid] = None
         s.table = []
+        s.np_table, s.np_copied = None, 0
 
     def preempt(self, s: Seq) -> None:
         self.release(s)
@@ -262,6 +265,7 @@ class StepStats:
     tokens: int        # query tokens in the step
     new_tokens: int    # sampled tokens emitted
     seconds: float
+    kv_tokens: int = 0  # keys the step's rows attend over (sum of k_len)
 
 
 class E2EEngine:
@@ -269,8 +273,9 @@ class E2EEngine:
 
     num_blocks, max_num_batched_tokens, max_num_seqs and min_chunk_size mean what
     they mean for the reference's LLMEngine (engine.py:18-61). ``trace`` records
-    every step's schedule: per row (request id, "P" or "D", chunk, computed
-    tokens before the step, block table) and the ids preempted.
+    every step's schedule (record_trace, on by default): per row (request id, "P"
+    or "D", chunk, computed tokens before the step, block table) and the ids
+    preempted.
     """
 
     GRAPH_BUCKETS = (1, 2, 4, 8, 16, 32, 64, 128, 256)
@@ -278,7 +283,7 @@ class E2EEngine:
     def __init__(self, model, num_blocks: int, max_num_batched_tokens: int | None = None,
                  max_num_seqs: int | None = None, min_chunk_size: int | None = None,
                  attn_implementation: str = PAGED_B200_ATTN_IMPL, use_graphs: bool = False,
-                 max_context: int = 8192, record_logits: bool = False):
+                 max_context: int = 8192, record_logits: bool = False, record_trace: bool = True):
         if attn_implementation == PAGED_B200_ATTN_IMPL:
             register()
         model.set_attn_implementation(attn_implementation)
@@ -303,6 +308,7 @@ class E2EEngine:
         self.stats: list[StepStats] = []
         self.trace: list[dict] = []
         self.record_logits = record_logits
+        self.record_trace = record_trace
         self.logit_log: list[tuple] = []  # (rid, output index, top-5 ids, top-5 logits) when recording
 
     @property
@@ -321,14 +327,16 @@ class E2EEngine:
         """One engine iteration; returns the number of tokens sampled."""
         t0 = time.perf_counter()
         plan = self.sched.plan()
-        self.trace.append({
-            "rows": [[s.rid, "D" if c is None else "P", 0 if c is None else c, s.computed, list(s.table)]
-                     for s, c in plan.rows],
-            "preempted": [s.rid for s in plan.preempted]})
+        if self.record_trace:
+            self.trace.append({
+                "rows": [[s.rid, "D" if c is None else "P", 0 if c is None else c, s.computed, list(s.table)]
+                         for s, c in plan.rows],
+                "preempted": [s.rid for s in plan.preempted]})
         if not plan.rows:
             self.stats.append(StepStats("idle", 0, 0, time.perf_counter() - t0))
             return 0
         n_tokens = sum(1 if c is None else max(c, 1) for _, c in plan.rows)
+        kv_tokens = sum(s.total_len if c is None else max(s.computed + c, 1) for s, c in plan.rows)
         if (self.graphs and not self.record_logits and all(c is None for _, c in plan.rows)
                 and len(plan.rows) <= max(self.graphs)):
             next_tok = self._graph_decode(plan.rows)
@@ -343,7 +351,7 @@ class E2EEngine:
             self.done.append(s)
         kinds = {"decode" if c is None else "prefill" for _, c in plan.rows}
         self.stats.append(StepStats("mixed" if len(kinds) > 1 else kinds.pop(), n_tokens, emitted,
-                                    time.perf_counter() - t0))
+                                    time.perf_counter() - t0, kv_tokens))
         return emitted
 
     def _eager_step(self, rows) -> list:
@@ -392,25 +400,41 @@ class E2EEngine:
         st["last"] = torch.arange(bucket, device=dev)
         return st
 
+    def _np_table(self, s: Seq) -> np.ndarray:
+        """The request's block table as int32, copied incrementally: a table only
+        grows by appends until BlockPool.release empties it (and drops the copy)."""
+        n = len(s.table)
+        if n > self.width:
+            raise ValueError(f"request of {s.total_len} tokens exceeds max_context {self.width * BLOCK_SIZE}")
+        if s.np_table is None:
+            s.np_table = np.zeros(self.width, dtype=np.int32)
+            s.np_copied = 0
+        if s.np_copied < n:
+            s.np_table[s.np_copied:n] = s.table[s.np_copied:n]
+            s.np_copied = n
+        return s.np_table
+
     def _load_graph_inputs(self, st: dict, rows) -> None:
         """Real rows first, then pad rows on the scratch block."""
         bucket = st["last"].numel()
+        b = len(rows)
         h = st["host"].numpy()
         k_lens = np.ones(bucket, dtype=np.int32)
         tables = np.zeros((bucket, self.width), dtype=np.int32)
-        tables[:, 0] = self.scratch_block
-        h[0, :] = 0
-        h[1, :] = 0
-        h[2, :] = self.scratch_block * BLOCK_SIZE
-        for i, (s, _) in enumerate(rows):
-            if len(s.table) > self.width:
-                raise ValueError(f"request of {s.total_len} tokens exceeds max_context {self.width * BLOCK_SIZE}")
-            p = s.total_len - 1
-            tables[i, :len(s.table)] = s.table
-            h[0, i] = s.out[-1]
-            h[1, i] = p
-            h[2, i] = s.table[p // BLOCK_SIZE] * BLOCK_SIZE + p % BLOCK_SIZE
-            k_lens[i] = s.total_len
+        tables[b:, 0] = self.scratch_block
+        h[:, b:] = 0
+        h[2, b:] = self.scratch_block * BLOCK_SIZE
+        if b:
+            seqs = [s for s, _ in rows]
+            tot = np.fromiter((s.total_len for s in seqs), dtype=np.int64, count=b)
+            pos = tot - 1
+            for i, s in enumerate(seqs):
+                tables[i] = self._np_table(s)
+            blk = tables[np.arange(b), pos // BLOCK_SIZE].astype(np.int64)
+            h[0, :b] = np.fromiter((s.out[-1] for s in seqs), dtype=np.int64, count=b)
+            h[1, :b] = pos
+            h[2, :b] = blk * BLOCK_SIZE + pos % BLOCK_SIZE
+            k_lens[:b] = tot
         st["dev"].copy_(st["host"], non_blocking=True)
         st["md"].update(k_lens, tables)
 
@@ -460,7 +484,7 @@ class E2EEngine:
     def run(self, max_idle_steps: int = 1000) -> None:
         idle = 0
         while self.has_unfinished():
-            if self.step() == 0 and not self.trace[-1]["rows"]:
+            if self.step() == 0 and self.stats[-1].kind == "idle":
                 idle += 1
                 if idle > max_idle_steps:
                     raise RuntimeError("no request can be scheduled: the pool is too small")

@@ -226,6 +226,44 @@ class TPLlamaDecoder:
             h = ar(nxt, cfg.eps)
         return h @ self.lm_head.t()
 
+    @torch.inference_mode()
+    def reference_logits(self, tokens: torch.Tensor) -> torch.Tensor:
+        """The same decode step in fp32 with dense attention over each row's
+        gathered context, for an unsharded decoder (world 1: it holds every
+        weight and kv head). The new token's K/V (rounded to the pool's bf16) is
+        written to a copy of the pool at the row's slot, as the step writes it;
+        the decoder's own pool is left untouched."""
+        if self.world != 1:
+            raise ValueError("reference_logits needs the unsharded (world 1) decoder")
+        cfg, b, d = self.cfg, self.batch, self.cfg.head_dim
+        g = cfg.heads // cfg.kv_heads
+        x = F.embedding(tokens, self.embed).float()
+        cos, sin = self.cos.float(), self.sin.float()
+        for li, w in enumerate(self.layers):
+            h = F.rms_norm(x, (cfg.hidden,), w["n1"].float(), cfg.eps)
+            qkv = h @ w["wqkv"].float().t()
+            q = self._rope(qkv[:, :cfg.heads * d].view(b, cfg.heads, d), cos, sin)
+            k = self._rope(qkv[:, cfg.heads * d:(cfg.heads + cfg.kv_heads) * d].view(b, cfg.kv_heads, d), cos, sin)
+            v = qkv[:, (cfg.heads + cfg.kv_heads) * d:].view(b, cfg.kv_heads, d)
+            kc = self.kv[li, 0].float().view(-1, cfg.kv_heads, d)
+            vc = self.kv[li, 1].float().view(-1, cfg.kv_heads, d)
+            kc[self.slots] = k.to(torch.bfloat16).float()
+            vc[self.slots] = v.to(torch.bfloat16).float()
+            slots = (self.block_table.long()[:, :, None] * BLOCK_SIZE
+                     + torch.arange(BLOCK_SIZE, device=x.device)).view(b, -1)[:, :self.context]
+            ks, vs = kc[slots], vc[slots]  # [b, context, kv heads, d]
+            ks = ks.repeat_interleave(g, dim=2)
+            vs = vs.repeat_interleave(g, dim=2)
+            sc = torch.einsum("bhd,bthd->bht", q, ks) * self.scale
+            o = torch.einsum("bht,bthd->bhd", torch.softmax(sc, dim=-1), vs)
+            x = x + o.reshape(b, -1) @ w["wo"].float().t()
+            h = F.rms_norm(x, (cfg.hidden,), w["n2"].float(), cfg.eps)
+            gu = h @ w["wgu"].float().t()
+            f = gu.shape[1] // 2
+            x = x + (F.silu(gu[:, :f]) * gu[:, f:]) @ w["wd"].float().t()
+        h = F.rms_norm(x, (cfg.hidden,), self.final_norm.float(), cfg.eps)
+        return h @ self.lm_head.float().t()
+
     def capture(self, warmup: int = 2) -> None:
         """Record one decode step into a CUDA graph (after eager warm-up steps)."""
         s = torch.cuda.Stream(device=self.device)

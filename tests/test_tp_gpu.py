@@ -3,7 +3,6 @@ down_proj) against a dense fp32 torch restatement of the same model, CUDA-graph
 replay against eager execution, and TP=2 against TP=1 when two GPUs exist, with
 the peer-memory all-reduce + add + RMSNorm kernel giving the same logits as
 NCCL followed by the add + norm kernel."""
-import math
 import os
 import socket
 
@@ -20,47 +19,6 @@ pytestmark = pytest.mark.gpu
 SMALL = TPConfig(layers=2, hidden=512, heads=8, kv_heads=4, head_dim=64, ffn=1024, vocab=1000)
 
 
-def dense_reference_logits(dec: TPLlamaDecoder, tokens: torch.Tensor) -> torch.Tensor:
-    """The same decode step in fp32 with dense attention over each sequence's
-    gathered context (world-1 decoder: it holds every weight and kv head)."""
-    cfg, b, d = dec.cfg, dec.batch, cfg_d(dec)
-    x = F.embedding(tokens, dec.embed).float()
-    kv = dec.kv.float().clone()
-    for li, w in enumerate(dec.layers):
-        h = F.rms_norm(x, (cfg.hidden,), w["n1"].float(), cfg.eps)
-        qkv = h @ w["wqkv"].float().t()
-        q = qkv[:, :cfg.heads * d].view(b, cfg.heads, d)
-        k = qkv[:, cfg.heads * d:(cfg.heads + cfg.kv_heads) * d].view(b, cfg.kv_heads, d)
-        v = qkv[:, (cfg.heads + cfg.kv_heads) * d:].view(b, cfg.kv_heads, d)
-        q = dec._rope(q, dec.cos.float(), dec.sin.float())
-        k = dec._rope(k, dec.cos.float(), dec.sin.float())
-        kflat = kv[li, 0].view(-1, cfg.kv_heads, d)
-        vflat = kv[li, 1].view(-1, cfg.kv_heads, d)
-        kflat[dec.slots] = k.to(torch.bfloat16).float()
-        vflat[dec.slots] = v.to(torch.bfloat16).float()
-        o = torch.empty(b, cfg.heads, d, device=x.device)
-        g = cfg.heads // cfg.kv_heads
-        for r in range(b):
-            blocks = dec.block_table[r].long()
-            ks = kv[li, 0][blocks].reshape(-1, cfg.kv_heads, d)[: dec.context]
-            vs = kv[li, 1][blocks].reshape(-1, cfg.kv_heads, d)[: dec.context]
-            for hh in range(cfg.heads):
-                s = (ks[:, hh // g] @ q[r, hh].to(torch.bfloat16).float()) * dec.scale
-                o[r, hh] = torch.softmax(s, dim=0) @ vs[:, hh // g]
-        a = o.reshape(b, -1).to(torch.bfloat16).float() @ w["wo"].float().t()
-        x = x + a
-        h = F.rms_norm(x, (cfg.hidden,), w["n2"].float(), cfg.eps)
-        gu = h @ w["wgu"].float().t()
-        f = gu.shape[1] // 2
-        x = x + (F.silu(gu[:, :f]) * gu[:, f:]) @ w["wd"].float().t()
-    h = F.rms_norm(x, (cfg.hidden,), dec.final_norm.float(), cfg.eps)
-    return h @ dec.lm_head.float().t()
-
-
-def cfg_d(dec):
-    return dec.cfg.head_dim
-
-
 def test_tp1_decode_matches_dense_reference():
     dec = TPLlamaDecoder(SMALL, 0, 1, torch.device("cuda"), batch=6, context=300, seed=2)
     tokens = torch.randint(0, SMALL.vocab, (6,), generator=torch.Generator().manual_seed(1)).cuda()
@@ -68,7 +26,8 @@ def test_tp1_decode_matches_dense_reference():
     logits = dec.logits(tokens).float()
     check_device_errors()
     dec.kv.copy_(kv_before)
-    ref = dense_reference_logits(dec, tokens)
+    ref = dec.reference_logits(tokens)  # fp32, dense attention over the gathered context
+    assert torch.equal(dec.kv, kv_before)  # the reference leaves the decoder's pool alone
     cos = F.cosine_similarity(logits, ref, dim=-1)
     assert float(cos.min()) > 0.999, cos
     assert float((logits - ref).abs().max()) < 0.05 * float(ref.abs().max()) + 1e-3
