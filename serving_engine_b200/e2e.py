@@ -32,9 +32,15 @@ one device-to-host copy. A prefill row whose whole prompt was matched in the
 prefix cache (a chunk of 0 tokens) runs its last token again, which rewrites
 the same K/V; the reference reads an unrelated row's logits there. With
 use_graphs, decode-only steps replay a CUDA graph captured per padded
-batch-size bucket: the step's tokens, positions, slots, lengths and block
-tables go to fixed device buffers in two host-to-device copies, and pad rows
-attend over a scratch block placed after the engine's blocks.
+batch-size bucket: the step's positions, slots, lengths and block tables go to
+fixed device buffers from pinned staging, and pad rows attend over a scratch
+block placed after the engine's blocks. Such a step is launched without
+waiting for it: its sampled tokens stay on the device, where the next step
+gathers them as its input tokens, and reach the host (over placeholders in the
+requests' outputs) while the next step runs, so the host's scheduling of step
+i + 1 overlaps the GPU's step i. The schedule never needs a token value unless a
+request has an end-of-sequence token, and a step with prefill rows first waits
+for every pending token.
 """
 from __future__ import annotations
 
@@ -309,6 +315,7 @@ class E2EEngine:
         self.trace: list[dict] = []
         self.record_logits = record_logits
         self.record_trace = record_trace
+        self._pending: dict | None = None  # the newest graph step whose tokens are not on the host yet
         self.logit_log: list[tuple] = []  # (rid, output index, top-5 ids, top-5 logits) when recording
 
     @property
@@ -337,22 +344,48 @@ class E2EEngine:
             return 0
         n_tokens = sum(1 if c is None else max(c, 1) for _, c in plan.rows)
         kv_tokens = sum(s.total_len if c is None else max(s.computed + c, 1) for s, c in plan.rows)
+        previous = self._pending
         if (self.graphs and not self.record_logits and all(c is None for _, c in plan.rows)
                 and len(plan.rows) <= max(self.graphs)):
-            next_tok = self._graph_decode(plan.rows)
+            # decode-only step: launched without waiting; its tokens stay on the
+            # device (the next step reads them there) and reach the host while the
+            # next step runs
+            self._graph_decode(plan.rows, previous)
+            if any(s.eos is not None for s, _ in plan.rows):
+                self._drain()  # the end-of-sequence check below needs the values
+            emitted = len(plan.rows)
         else:
+            self._drain()  # a prefill row may need the real values of earlier tokens
+            previous = None
             next_tok = self._eager_step(plan.rows)
-        emitted = 0
-        for (s, c), tok in zip(plan.rows, next_tok):
-            if c is None or s.rid in plan.final:
-                s.out.append(int(tok))
-                emitted += 1
+            emitted = 0
+            for (s, c), tok in zip(plan.rows, next_tok):
+                if c is None or s.rid in plan.final:
+                    s.out.append(int(tok))
+                    emitted += 1
         for s in self.sched.commit(plan):
             self.done.append(s)
+        if previous is not None and previous is not self._pending:
+            self._drain(previous)
+        if self._pending is not None and not self.sched.has_unfinished():
+            self._drain()  # nothing left to run: the caller may read every output now
         kinds = {"decode" if c is None else "prefill" for _, c in plan.rows}
         self.stats.append(StepStats("mixed" if len(kinds) > 1 else kinds.pop(), n_tokens, emitted,
                                     time.perf_counter() - t0, kv_tokens))
         return emitted
+
+    def _drain(self, pending: dict | None = None) -> None:
+        """Wait for a launched graph step's tokens (default: the newest) and write
+        them over its placeholders."""
+        pending = self._pending if pending is None else pending
+        if pending is None:
+            return
+        pending["event"].synchronize()
+        values = pending["host"][:len(pending["rows"])].tolist()
+        for (s, idx), v in zip(pending["rows"], values):
+            s.out[idx] = v
+        if pending is self._pending:
+            self._pending = None
 
     def _eager_step(self, rows) -> list:
         toks, pos, slots = [], [], []
@@ -393,11 +426,20 @@ class E2EEngine:
 
     # ------------------------------------------------------------ CUDA graphs
     def _graph_inputs(self, bucket: int) -> dict:
+        """Fixed device buffers a bucket's graph reads: rows 0-2 of ``dev`` are the
+        tokens, positions and write slots. Host staging is pinned and used in
+        turn (``host``: tokens, positions, slots and, in row 3, where each token
+        comes from: -1 for the host value, else its row in the previous step's
+        device output)."""
         dev = self.device
-        st = {"host": torch.zeros(3, bucket, dtype=torch.int64).pin_memory()}
-        st["dev"] = st["host"].to(dev)
+        st = {"hosts": [torch.zeros(4, bucket, dtype=torch.int64).pin_memory() for _ in range(2)],
+              "copied": [None, None], "turn": 0}
+        st["host"] = st["hosts"][0]
+        st["dev"] = torch.zeros(3, bucket, dtype=torch.int64, device=dev)
+        st["src"] = torch.zeros(bucket, dtype=torch.int64, device=dev)
         st["md"] = DecodeMetadataBuffer(bucket, self.width, dev)
         st["last"] = torch.arange(bucket, device=dev)
+        st["tokens_host"] = [torch.zeros(bucket, dtype=torch.int64).pin_memory() for _ in range(2)]
         return st
 
     def _np_table(self, s: Seq) -> np.ndarray:
@@ -414,16 +456,25 @@ class E2EEngine:
             s.np_copied = n
         return s.np_table
 
-    def _load_graph_inputs(self, st: dict, rows) -> None:
-        """Real rows first, then pad rows on the scratch block."""
+    def _load_graph_inputs(self, st: dict, rows, previous: dict | None = None) -> None:
+        """Real rows first, then pad rows on the scratch block. A row whose newest
+        token is still a placeholder of the previous (graph) step takes it from
+        that step's device output."""
         bucket = st["last"].numel()
         b = len(rows)
+        k = st["turn"]
+        st["turn"] ^= 1
+        if st["copied"][k] is not None:
+            st["copied"][k].synchronize()  # its previous copy to the device has run
+        st["host"] = st["hosts"][k]
         h = st["host"].numpy()
         k_lens = np.ones(bucket, dtype=np.int32)
         tables = np.zeros((bucket, self.width), dtype=np.int32)
         tables[b:, 0] = self.scratch_block
         h[:, b:] = 0
         h[2, b:] = self.scratch_block * BLOCK_SIZE
+        h[3, :] = -1
+        gather = False
         if b:
             seqs = [s for s, _ in rows]
             tot = np.fromiter((s.total_len for s in seqs), dtype=np.int64, count=b)
@@ -431,11 +482,28 @@ class E2EEngine:
             for i, s in enumerate(seqs):
                 tables[i] = self._np_table(s)
             blk = tables[np.arange(b), pos // BLOCK_SIZE].astype(np.int64)
-            h[0, :b] = np.fromiter((s.out[-1] for s in seqs), dtype=np.int64, count=b)
+            prev_row = previous["row_of"] if previous is not None else {}
+            toks = np.empty(b, dtype=np.int64)
+            for i, s in enumerate(seqs):
+                t = s.out[-1]
+                if t is None:  # produced by the previous step, still on the device
+                    h[3, i] = prev_row[s.rid]
+                    toks[i] = 0
+                    gather = True
+                else:
+                    toks[i] = t
+            h[0, :b] = toks
             h[1, :b] = pos
             h[2, :b] = blk * BLOCK_SIZE + pos % BLOCK_SIZE
             k_lens[:b] = tot
-        st["dev"].copy_(st["host"], non_blocking=True)
+        st["dev"].copy_(st["host"][:3], non_blocking=True)
+        if gather:
+            st["src"].copy_(st["host"][3], non_blocking=True)
+            picked = previous["st"]["out"].index_select(0, st["src"].clamp(min=0))
+            st["dev"][0].copy_(torch.where(st["src"] >= 0, picked, st["dev"][0]))
+        ev = torch.cuda.Event()
+        ev.record()
+        st["copied"][k] = ev
         st["md"].update(k_lens, tables)
 
     def _run_graph_body(self, st: dict):
@@ -471,12 +539,24 @@ class E2EEngine:
             self.graphs[bucket] = st
         torch.cuda.synchronize(self.device)
 
-    def _graph_decode(self, rows) -> list:
+    def _graph_decode(self, rows, previous: dict | None) -> None:
+        """Replay the bucket's graph for a decode-only step without waiting for it:
+        each row gets a placeholder token, filled in by _drain once the step's
+        tokens are on the host."""
         bucket = min(b for b in self.graphs if b >= len(rows))
         st = self.graphs[bucket]
-        self._load_graph_inputs(st, rows)
+        self._load_graph_inputs(st, rows, previous)
         st["graph"].replay()
-        return st["out"][:len(rows)].tolist()
+        host = st["tokens_host"][st["turn"]]
+        host[:len(rows)].copy_(st["out"][:len(rows)], non_blocking=True)
+        ev = torch.cuda.Event()
+        ev.record()
+        placed = []
+        for s, _ in rows:
+            placed.append((s, len(s.out)))
+            s.out.append(None)
+        self._pending = {"rows": placed, "host": host, "event": ev, "st": st,
+                         "row_of": {s.rid: i for i, (s, _) in enumerate(rows)}}
 
     def has_unfinished(self) -> bool:
         return self.sched.has_unfinished()

@@ -170,8 +170,8 @@ class DecodeMetadataBuffer:
     def __init__(self, rows: int, width: int, device):
         self.rows, self.width = rows, width
         n = 4 * rows + rows * width + 3 * rows
-        self.host = torch.zeros(n, dtype=torch.int32).pin_memory()
-        a = self.host.numpy()
+        host = torch.zeros(n, dtype=torch.int32)
+        a = host.numpy()
         ar = np.arange(rows, dtype=np.int32)
         a[0:rows] = 1
         a[2 * rows:3 * rows] = ar
@@ -179,6 +179,12 @@ class DecodeMetadataBuffer:
         a[o:o + rows] = ar          # item_row
         a[o + rows:o + 2 * rows] = ar  # decode tokens
         a[o + 2 * rows:o + 3 * rows] = ar  # decode rows
+        # two pinned staging copies, used in turn: a step's update may be written
+        # while the previous step's copy to the device is still in flight
+        self._hosts = [host.pin_memory(), host.clone().pin_memory()]
+        self._copied = [None, None]
+        self._turn = 0
+        self.host = self._hosts[0]
         self.dev = self.host.to(device)
         buf, r, w = self.dev, rows, width
         self.metadata = {
@@ -191,14 +197,23 @@ class DecodeMetadataBuffer:
         }
 
     def update(self, k_lens: np.ndarray, tables: np.ndarray) -> None:
-        """Write this step's k_lens [rows] and block tables [rows, width] (host
-        side, pinned), then copy the buffer to the device asynchronously."""
+        """Write this step's k_lens [rows] and block tables [rows, width] into a
+        pinned staging copy (waiting, if needed, until its previous copy to the
+        device has run), then copy it to the device on the current stream."""
         r, w = self.rows, self.width
+        k = self._turn
+        self._turn ^= 1
+        if self._copied[k] is not None:
+            self._copied[k].synchronize()
+        self.host = self._hosts[k]
         a = self.host.numpy()
         a[r:2 * r] = k_lens
         a[3 * r:4 * r] = k_lens - 1
         a[4 * r:4 * r + r * w] = tables.reshape(-1)
         self.dev.copy_(self.host, non_blocking=True)
+        ev = torch.cuda.Event()
+        ev.record()
+        self._copied[k] = ev
 
 
 def metadata_from_lists(q_lens, k_lens, q_starts, q_pos_offsets, tables, device="cuda") -> dict:

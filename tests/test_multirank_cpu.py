@@ -36,9 +36,9 @@ def test_shard_spec_and_max_over_ranks_gloo(world):
     procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
     for p in procs:
         p.start()
-    results = sorted(q.get(timeout=120) for _ in procs)
+    results = sorted(q.get(timeout=300) for _ in procs)
     for p in procs:
-        p.join(timeout=60)
+        p.join(timeout=120)
         assert p.exitcode == 0
     assert [r[2] for r in results] == [10.0 + world - 1] * world  # every rank sees the slowest time
     specs = [r[1] for r in results]
@@ -79,9 +79,9 @@ def test_tp_mlp_shards_sum_to_full_mlp_gloo():
     procs = [ctx.Process(target=_tp_mlp_worker, args=(r, 2, port, q)) for r in range(2)]
     for p in procs:
         p.start()
-    outs = dict(q.get(timeout=120) for _ in procs)
+    outs = dict(q.get(timeout=300) for _ in procs)
     for p in procs:
-        p.join(timeout=60)
+        p.join(timeout=120)
         assert p.exitcode == 0
     cfg = TPConfig(layers=1, hidden=64, heads=4, kv_heads=2, head_dim=16, ffn=96, vocab=50)
     full = TPLlamaDecoder(cfg, 0, 1, torch.device("cpu"), batch=3, context=20, seed=5, fill_kv=False)
@@ -99,9 +99,12 @@ def _leaving_worker(rank, world, port, q):
     import time
 
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
-    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=3))
+    # a slow-starting rank must not fail the rendezvous: only the collectives'
+    # group carries the short timeout
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120))
+    group = dist.new_group(list(range(world)), timeout=datetime.timedelta(seconds=3))
     t = torch.ones(4)
-    dist.all_reduce(t)  # one step together
+    dist.all_reduce(t, group=group)  # one step together
     if rank == 1:
         q.put((rank, "left", float(t[0])))
         q.close()
@@ -109,7 +112,7 @@ def _leaving_worker(rank, world, port, q):
         os._exit(0)  # leave without the next collective or a clean shutdown
     t0 = time.monotonic()
     try:
-        dist.all_reduce(t)
+        dist.all_reduce(t, group=group)
         q.put((rank, "no error", time.monotonic() - t0))
     except Exception as e:  # noqa: BLE001 - the backend's error type varies
         q.put((rank, f"error: {type(e).__name__}", time.monotonic() - t0))
@@ -125,9 +128,9 @@ def test_rank_leaving_ends_peer_collective_with_error():
     procs = [ctx.Process(target=_leaving_worker, args=(r, 2, port, q)) for r in range(2)]
     for p in procs:
         p.start()
-    outs = dict((r, (msg, v)) for r, msg, v in (q.get(timeout=120) for _ in procs))
+    outs = dict((r, (msg, v)) for r, msg, v in (q.get(timeout=300) for _ in procs))
     for p in procs:
-        p.join(timeout=60)
+        p.join(timeout=120)
         assert p.exitcode == 0
     assert outs[1][0] == "left" and outs[1][1] == 2.0
     msg, waited = outs[0]
