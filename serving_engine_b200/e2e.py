@@ -281,7 +281,10 @@ class E2EEngine:
     they mean for the reference's LLMEngine (engine.py:18-61). ``trace`` records
     every step's schedule (record_trace, on by default): per row (request id, "P"
     or "D", chunk, computed tokens before the step, block table) and the ids
-    preempted.
+    preempted. With fused_decode (bf16 / fp16 models, with use_graphs), the
+    captured decode steps run the model through the fused layer kernels
+    (llama_decode.FusedLlamaDecode) instead of its HF modules; prefill and mixed
+    steps always run the HF modules.
     """
 
     GRAPH_BUCKETS = (1, 2, 4, 8, 16, 32, 64, 128, 256)
@@ -289,7 +292,8 @@ class E2EEngine:
     def __init__(self, model, num_blocks: int, max_num_batched_tokens: int | None = None,
                  max_num_seqs: int | None = None, min_chunk_size: int | None = None,
                  attn_implementation: str = PAGED_B200_ATTN_IMPL, use_graphs: bool = False,
-                 max_context: int = 8192, record_logits: bool = False, record_trace: bool = True):
+                 max_context: int = 8192, record_logits: bool = False, record_trace: bool = True,
+                 fused_decode: bool = False):
         if attn_implementation == PAGED_B200_ATTN_IMPL:
             register()
         model.set_attn_implementation(attn_implementation)
@@ -316,6 +320,12 @@ class E2EEngine:
         self.record_logits = record_logits
         self.record_trace = record_trace
         self._pending: dict | None = None  # the newest graph step whose tokens are not on the host yet
+        # graph-captured decode steps through the fused layer kernels instead of the HF modules
+        self.fused = None
+        if fused_decode:
+            from .llama_decode import FusedLlamaDecode
+
+            self.fused = FusedLlamaDecode(model)
         self.logit_log: list[tuple] = []  # (rid, output index, top-5 ids, top-5 logits) when recording
 
     @property
@@ -508,6 +518,8 @@ class E2EEngine:
 
     def _run_graph_body(self, st: dict):
         d = st["dev"]
+        if self.fused is not None:
+            return self.fused.logits(d[0], d[1], d[2], self.kv_cache, st["md"].metadata).argmax(dim=-1)
         out = self.model(input_ids=d[0].unsqueeze(0), position_ids=d[1].unsqueeze(0), attention_mask=None,
                          past_key_values=None, use_cache=False, cache=self.cache, write_index=d[2],
                          paged_metadata=st["md"].metadata, logits_to_keep=st["last"])

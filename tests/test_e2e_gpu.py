@@ -52,10 +52,10 @@ def test_greedy_tokens_match_reference_engine(golden_meta, graphs):
         assert any(st.kind == "decode" for st in eng.stats)
 
 
-def run_config4(model, w, graphs=False, record_logits=False):
+def run_config4(model, w, graphs=False, record_logits=False, fused=False):
     eng = E2EEngine(model, num_blocks=w["num_gpu_blocks"], max_num_batched_tokens=w["max_num_batched_tokens"],
                     max_num_seqs=w["max_num_seqs"], min_chunk_size=w["min_chunk_size"], use_graphs=graphs,
-                    max_context=512, record_logits=record_logits)
+                    max_context=512, record_logits=record_logits, fused_decode=fused)
     if graphs:
         eng.capture_graphs(buckets=[1, 2, 4, 8, 16])
     last = max(w["arrivals"])
@@ -93,16 +93,85 @@ def test_config4_shape_schedule_and_tokens_match_reference_engine(golden_meta, c
         assert any(st.kind == "decode" for st in eng.stats)
 
 
-def test_config4_shape_bf16_divergence_is_near_tie(golden_meta, golden_arrays, config4_fp32):
+@pytest.fixture(scope="module")
+def config4_bf16(config4_fp32):
+    return copy.deepcopy(config4_fp32).to(torch.bfloat16)  # the same weights, rounded to bf16
+
+
+def test_config4_shape_bf16_divergence_is_near_tie(golden_meta, golden_arrays, config4_bf16):
+    eng = run_config4(config4_bf16, e2e_config4_workload(), record_logits=True)
+    triage_against_fp32(golden_meta, golden_arrays, eng, {(rid, n): (ids, vals)
+                                                        for rid, n, ids, vals in eng.logit_log})
+
+
+def test_config4_shape_bf16_fused_graph_decode(golden_meta, golden_arrays, config4_bf16):
+    """Decode steps replayed from graphs of the fused layer kernels
+    (llama_decode.FusedLlamaDecode), prefill steps through the HF modules: the
+    same schedule, and the same near-tie triage against the fp32 reference. The
+    fused path's logits are not recorded, so the triage uses the HF path's
+    logits at the first diverging token; a fused decode divergence that is not a
+    near-tie shows up as tokens leaving the HF bf16 run's far from a tie."""
+    w = e2e_config4_workload()
+    eng = run_config4(config4_bf16, w, graphs=True, fused=True)
+    assert eng.trace == golden_meta["e2e_config4_fp32"]["trace"]
+    assert any(st.kind == "decode" for st in eng.stats)
+    hf = run_config4(config4_bf16, w, record_logits=True)
+    hf_at = {(rid, n): (ids, vals) for rid, n, ids, vals in hf.logit_log}
+    agree = sum(a == b for s, t in zip(eng.seqs, hf.seqs) for a, b in zip(s.out, t.out))
+    assert agree >= 0.5 * sum(len(s.out) for s in eng.seqs)
+    for s, t in zip(eng.seqs, hf.seqs):
+        n = next((i for i, (a, b) in enumerate(zip(s.out, t.out)) if a != b), None)
+        if n is None:
+            continue
+        ids, vals = hf_at[(s.rid, n)]
+        assert s.out[n] in ids, f"request {s.rid}: fused token {s.out[n]} not in the HF top-5 {ids}"
+        margin = vals[0] - vals[ids.index(s.out[n])]
+        assert margin <= 0.1, f"request {s.rid} output {n}: HF margin {margin} is no near-tie"
+
+
+def test_fused_decode_logits_match_hf_modules():
+    """One decode step on the same pool state through the HF modules and through
+    FusedLlamaDecode: the logits agree to bf16 rounding noise."""
+    from serving_engine_b200.llama_decode import FusedLlamaDecode
+    from serving_engine_b200.paged_attention import metadata_from_lists
+
+    model = random_llama("tiny", seed=4, dtype=torch.bfloat16, device="cuda")
+    eng = E2EEngine(model, num_blocks=128, max_num_batched_tokens=256)
+    for p in config4_requests(seed=5, n=6, vocab=1000):
+        eng.add_request(p[:30 + len(p) % 50], 3)
+    while any(not s.decoding for s in eng.seqs):  # prefill everything
+        eng.step()
+    seqs = [s for s in eng.seqs if s.decoding and s.status == "running"]
+    for s in seqs:
+        eng.pool.grow(s)
+    pos = [s.total_len - 1 for s in seqs]
+    slots = [s.table[p // 16] * 16 + p % 16 for s, p in zip(seqs, pos)]
+    dev = torch.device("cuda")
+    ids = torch.tensor([s.out[-1] for s in seqs], device=dev)
+    pos_t = torch.tensor(pos, device=dev)
+    slot_t = torch.tensor(slots, device=dev)
+    md = metadata_from_lists([1] * len(seqs), [p + 1 for p in pos], list(range(len(seqs))), pos,
+                             [s.table for s in seqs], dev)
+    snapshot = eng.kv_cache.clone()
+    with torch.inference_mode():
+        ref = model(input_ids=ids[None], position_ids=pos_t[None], attention_mask=None, past_key_values=None,
+                    use_cache=False, cache=eng.cache, write_index=slot_t, paged_metadata=md,
+                    logits_to_keep=torch.arange(len(seqs), device=dev)).logits[0].float()
+        eng.kv_cache.copy_(snapshot)
+        fused = FusedLlamaDecode(model).logits(ids, pos_t, slot_t, eng.kv_cache, md).float()
+    check_device_errors()
+    cos = torch.nn.functional.cosine_similarity(fused, ref, dim=-1)
+    assert float(cos.min()) > 0.9999, cos
+    assert float((fused - ref).abs().max()) < 0.02 * float(ref.abs().max())
+
+
+def triage_against_fp32(golden_meta, golden_arrays, eng, ours_at):
     g = golden_meta["e2e_config4_fp32"]
     w = e2e_config4_workload()
-    model = copy.deepcopy(config4_fp32).to(torch.bfloat16)  # the same weights, rounded to bf16
-    eng = run_config4(model, w, record_logits=True)
     assert eng.trace == g["trace"]  # the schedule does not depend on token values
     ref_ids = golden_arrays["e2e_config4_fp32__top5_ids"]
     ref_vals = golden_arrays["e2e_config4_fp32__top5_logits"]
     ref_at = {tuple(k): i for i, k in enumerate(g["sampled"])}
-    ours_at = {(rid, n): (ids, vals) for rid, n, ids, vals in eng.logit_log}
     # bf16 logit noise: |ours - reference| on the tokens both top-5 lists hold, at
     # every request's first sampled token (identical contexts there)
     noise = 0.0
