@@ -139,3 +139,39 @@ def test_peer_memory_calls_reject_null(lib):
     assert lib.seb_peer_alloc(0, None) == _lib.SEB_EINVAL
     assert lib.seb_peer_export(None, None) == _lib.SEB_EINVAL
     assert lib.seb_peer_import(None, None) == _lib.SEB_EINVAL
+
+
+def test_paged_attention_workspace_size(lib):
+    """The routed entry point's workspace: the routing region (two counts, decode
+    items' tokens and rows, the prefill unit list bounded by the host-known
+    sizes), rounded to 256 bytes, then the split-K decode workspace for
+    max(rows, total_query) items."""
+    assert lib.seb_paged_attention_workspace_size(0, 10, 32, 8, 128, 64) == 0
+    assert lib.seb_paged_attention_workspace_size(5, 0, 32, 8, 128, 64) == 0
+    assert lib.seb_paged_attention_workspace_size(5, 100, 30, 8, 128, 64) == 0  # heads not a multiple
+    rows, tq, hq, hkv, d, mb = 7, 1000, 32, 8, 128, 200
+    pair_queries = 2 * (128 // (hq // hkv))
+    cap = hkv * (tq // pair_queries + min(rows, tq // 2))
+    route = 16 + 8 * rows + 8 * cap
+    route = -(-route // 256) * 256
+    decode = lib.seb_paged_decode_workspace_size(max(rows, tq), hq, hkv, d, mb, 0)
+    assert lib.seb_paged_attention_workspace_size(rows, tq, hq, hkv, d, mb) == route + decode
+
+
+def test_paged_attention_validation(lib):
+    """Rejected on the host before any launch: NULL metadata, a workspace smaller
+    than the size function reports, an unaligned workspace."""
+    assert lib.seb_paged_attention(None, 0, 0, None, None, 1, None, 4, 4, None, None, None, None, 0, 0, 32, 8, 128,
+                                   _lib.SEB_BF16, 0.1, 1, None, 0, 0, None, 0, None, 0, None, None) == _lib.SEB_OK
+    st = lib.seb_paged_attention(None, 0, 0, None, None, 1, None, 4, 4, None, None, None, None, 3, 9, 32, 8, 128,
+                                 _lib.SEB_BF16, 0.1, 1, None, 0, 0, None, 0, None, 0, None, None)
+    assert st == _lib.SEB_EINVAL and b"NULL metadata" in lib.seb_last_error()
+    fake = ctypes.c_void_p(4096)  # never dereferenced: the call returns before any launch
+    need = lib.seb_paged_attention_workspace_size(3, 9, 32, 8, 128, 4)
+    st = lib.seb_paged_attention(fake, 0, 0, fake, fake, 1, fake, 4, 4, fake, fake, fake, fake, 3, 9, 32, 8, 128,
+                                 _lib.SEB_BF16, 0.1, 1, fake, 0, 0, fake, 0, fake, need - 16, None, None)
+    assert st == _lib.SEB_EWORKSPACE
+    st = lib.seb_paged_attention(fake, 0, 0, fake, fake, 1, fake, 4, 4, fake, fake, fake, fake, 3, 9, 32, 8, 128,
+                                 _lib.SEB_BF16, 0.1, 1, fake, 0, 0, fake, 0, ctypes.c_void_p(4096 + 16), need,
+                                 None, None)
+    assert st == _lib.SEB_EWORKSPACE and b"256-byte aligned" in lib.seb_last_error()

@@ -217,3 +217,67 @@ def test_bf16_engine_runs_chunked_and_mixed_steps():
     assert all(0 <= t < 1000 for s in eng.done for t in s.out)
     assert {st.kind for st in eng.stats} >= {"mixed", "decode"}
     assert len(eng.free) == 256
+
+
+class _ReferenceStyleCache:
+    """What the reference's _PagedKVCache (serving_engine/model_runner.py:11-45)
+    offers the registered attention function: blocks(layer) and num_kv_heads."""
+
+    def __init__(self, kv_cache):
+        self.kv_cache = kv_cache
+        self.num_kv_heads = kv_cache.shape[-2]
+
+    def blocks(self, layer_idx):
+        return self.kv_cache[layer_idx, 0], self.kv_cache[layer_idx, 1]
+
+
+def test_reference_model_runner_inputs_give_the_same_logits():
+    """One mixed step (prefill chunks and decode rows) of the HF model through the
+    registered "paged|b200" function, fed the way the reference's
+    ModelRunner.forward feeds it (model_runner.py:168-209: write_index, a
+    metadata dict with the reference builder's keys only, its own cache object),
+    gives bit-identical logits and KV pool to the same step fed this package's
+    metadata and cache: the reference's dict is routed on the device."""
+    from serving_engine_b200.kv_cache import PagedKVCache, register
+    from serving_engine_b200.paged_attention import metadata_from_lists
+    from serving_engine_b200.workloads import PagedBatch
+
+    register()
+    model = random_llama("tiny", seed=6, dtype=torch.bfloat16, device="cuda")
+    model.set_attn_implementation("paged|b200")
+    cfg = model.config
+    dev = torch.device("cuda")
+    gen = torch.Generator().manual_seed(8)
+    rows = [(40, 0), (1, 77), (25, 16), (1, 300), (1, 5)]  # (q_len, num_computed)
+    tables, free = [], list(range(200))
+    for ql, qp in rows:
+        tables.append([free.pop() for _ in range(-(-(ql + qp) // 16))])
+    toks = torch.randint(0, cfg.vocab_size, (sum(r[0] for r in rows),), generator=gen)
+    pos = torch.cat([torch.arange(qp, qp + ql) for ql, qp in rows])
+    slots = torch.tensor([tables[i][p // 16] * 16 + p % 16 for i, (ql, qp) in enumerate(rows)
+                          for p in range(qp, qp + ql)])
+    q_starts = np.concatenate(([0], np.cumsum([r[0] for r in rows])[:-1])).tolist()
+    batch = PagedBatch(q=torch.empty(0), k_cache=torch.empty(0), v_cache=torch.empty(0), block_tables=tables,
+                       q_lens=[r[0] for r in rows], k_lens=[r[0] + r[1] for r in rows],
+                       q_pos_offsets=[r[1] for r in rows], num_q_heads=cfg.num_attention_heads,
+                       num_kv_heads=cfg.num_key_value_heads, scale=1.0)
+    pool0 = torch.randn(cfg.num_hidden_layers, 2, 200, 16, cfg.num_key_value_heads, cfg.head_dim,
+                        generator=gen).to(torch.bfloat16).to(dev)
+    last = torch.tensor(np.cumsum([r[0] for r in rows]) - 1, device=dev)
+    outs = {}
+    for mode in ("reference", "package"):
+        pool = pool0.clone()
+        if mode == "reference":
+            md, cache = batch.metadata(dev), _ReferenceStyleCache(pool)
+            assert "prefill_rows" not in md
+        else:
+            md = metadata_from_lists(batch.q_lens, batch.k_lens, q_starts, batch.q_pos_offsets, tables, dev)
+            cache = PagedKVCache(pool)
+        with torch.inference_mode():
+            logits = model(input_ids=toks.to(dev)[None], position_ids=pos.to(dev)[None], attention_mask=None,
+                           past_key_values=None, use_cache=False, cache=cache, write_index=slots.to(dev),
+                           paged_metadata=md, logits_to_keep=last).logits[0]
+        check_device_errors()
+        outs[mode] = (logits.float().cpu(), pool.cpu())
+    assert torch.equal(outs["reference"][0], outs["package"][0])
+    assert torch.equal(outs["reference"][1].view(torch.int16), outs["package"][1].view(torch.int16))
