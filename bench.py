@@ -60,8 +60,8 @@ def parse_args():
     ap.add_argument("--no-e2e-decode", action="store_true",
                     help="decode line: skip the end-to-end decode tok/s sub-record (config 4 / config 5)")
     ap.add_argument("--no-prefill", action="store_true", help="decode line: skip the config-3 prefill sub-record")
-    ap.add_argument("--hf-decode", action="store_true",
-                    help="config 4: decode steps through the HF modules instead of the fused layer kernels")
+    ap.add_argument("--hf-model", action="store_true",
+                    help="config 4: every step through the HF modules instead of the fused layer kernels")
     ap.add_argument("--tp-context", type=int, default=4096)
     ap.add_argument("--no-graph", action="store_true", help="tp / e2e: run decode steps eagerly")
     ap.add_argument("--tp-allreduce", default="peer", choices=["peer", "nccl"],
@@ -675,9 +675,10 @@ def run_e2e_workload(args, device):
     (median 512, clipped to [32, 4096]) and 128 greedy tokens each, served with
     continuous batching through the registered "paged|b200" attention.
 
-    Decode-only steps run as pipelined CUDA graphs of the fused layer kernels
-    (llama_decode.FusedLlamaDecode; --hf-decode: of the HF modules) and are
-    reported with their HBM bytes: the weights read once per step plus every
+    Every step runs the model through the fused layer kernels over its own
+    weights (llama_step.FusedLlamaStep; --hf-model: through the HF modules), the
+    decode-only steps as pipelined CUDA graphs, which are reported with their HBM
+    bytes: the weights read once per step plus every
     row's K/V (32 KiB per token) read by the attention of all 16 layers, against
     MEASURED_PEAKS.json hbm_gbs."""
     from serving_engine_b200 import ops
@@ -703,7 +704,7 @@ def run_e2e_workload(args, device):
     graphs = not args.no_graph
     eng = E2EEngine(model, num_blocks=num_blocks, max_num_batched_tokens=args.e2e_budget, max_num_seqs=256,
                     use_graphs=graphs, max_context=4096 + max_new, record_trace=False,
-                    fused_decode=graphs and not args.hf_decode)
+                    fused_steps=not args.hf_model)
     if graphs:
         eng.capture_graphs()
     for p in prompts:
@@ -733,8 +734,8 @@ def run_e2e_workload(args, device):
                    "prompt_tokens": sum(len(p) for p in prompts), "generated_tokens": gen,
                    "max_num_batched_tokens": args.e2e_budget, "max_num_seqs": 256,
                    "cuda_graph_decode": graphs,
-                   "decode_path": "fused layer kernels" if eng.fused is not None else "HF modules",
-                   "prefill_path": "HF modules with the registered paged|b200 attention"},
+                   "model_path": ("fused layer kernels over the HF model's weights (llama_step.FusedLlamaStep)"
+                                  if eng.fused is not None else "HF modules with the registered paged|b200 attention")},
         "wall_s": round(wall, 3),
         "decode_only": {"tokens_per_s": round(dec_tok / dec_s, 1) if dec_s else None, "steps": len(dec),
                         "ms_per_step": round(dec_s / max(len(dec), 1) * 1e3, 3),

@@ -281,10 +281,9 @@ class E2EEngine:
     they mean for the reference's LLMEngine (engine.py:18-61). ``trace`` records
     every step's schedule (record_trace, on by default): per row (request id, "P"
     or "D", chunk, computed tokens before the step, block table) and the ids
-    preempted. With fused_decode (bf16 / fp16 models, with use_graphs), the
-    captured decode steps run the model through the fused layer kernels
-    (llama_decode.FusedLlamaDecode) instead of its HF modules; prefill and mixed
-    steps always run the HF modules.
+    preempted. With fused_steps (bf16 / fp16 models), every step, the captured
+    decode graphs included, runs the model through the fused layer kernels
+    (llama_step.FusedLlamaStep) over its own weights instead of its HF modules.
     """
 
     GRAPH_BUCKETS = (1, 2, 4, 8, 16, 32, 64, 128, 256)
@@ -293,7 +292,7 @@ class E2EEngine:
                  max_num_seqs: int | None = None, min_chunk_size: int | None = None,
                  attn_implementation: str = PAGED_B200_ATTN_IMPL, use_graphs: bool = False,
                  max_context: int = 8192, record_logits: bool = False, record_trace: bool = True,
-                 fused_decode: bool = False):
+                 fused_steps: bool = False):
         if attn_implementation == PAGED_B200_ATTN_IMPL:
             register()
         model.set_attn_implementation(attn_implementation)
@@ -320,12 +319,12 @@ class E2EEngine:
         self.record_logits = record_logits
         self.record_trace = record_trace
         self._pending: dict | None = None  # the newest graph step whose tokens are not on the host yet
-        # graph-captured decode steps through the fused layer kernels instead of the HF modules
+        # steps through the fused layer kernels instead of the HF modules
         self.fused = None
-        if fused_decode:
-            from .llama_decode import FusedLlamaDecode
+        if fused_steps:
+            from .llama_step import FusedLlamaStep
 
-            self.fused = FusedLlamaDecode(model)
+            self.fused = FusedLlamaStep(model)
         self.logit_log: list[tuple] = []  # (rid, output index, top-5 ids, top-5 logits) when recording
 
     @property
@@ -422,10 +421,13 @@ class E2EEngine:
         slot_t = torch.from_numpy(np.concatenate(slots)).pin_memory().to(dev, non_blocking=True)
         md = PackedMetadata(q_lens, k_lens, starts, q_pos, [s.table for s, _ in rows]).upload(dev)
         last = torch.from_numpy(np.cumsum(q_lens) - 1).pin_memory().to(dev, non_blocking=True)
-        out = self.model(input_ids=ids.unsqueeze(0), position_ids=pos_t.unsqueeze(0), attention_mask=None,
-                         past_key_values=None, use_cache=False, cache=self.cache, write_index=slot_t,
-                         paged_metadata=md, logits_to_keep=last)
-        logits = out.logits[0]
+        if self.fused is not None:
+            logits = self.fused.logits(ids, pos_t, slot_t, self.kv_cache, md, last)
+        else:
+            out = self.model(input_ids=ids.unsqueeze(0), position_ids=pos_t.unsqueeze(0), attention_mask=None,
+                             past_key_values=None, use_cache=False, cache=self.cache, write_index=slot_t,
+                             paged_metadata=md, logits_to_keep=last)
+            logits = out.logits[0]
         if self.record_logits:
             top = torch.topk(logits.float(), 5, dim=-1)
             ids5, vals5 = top.indices.tolist(), top.values.tolist()

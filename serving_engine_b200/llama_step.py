@@ -1,23 +1,24 @@
-"""Decode steps of a Hugging Face Llama model through this library's fused layer
+"""Steps of a Hugging Face Llama model through this library's fused layer
 kernels, over the model's own weights and the engine's paged KV pool.
 
-A decode step of ``LlamaForCausalLM`` (transformers models/llama/modeling_llama.py)
-runs each layer as RMSNorm, q/k/v projections, rotary embedding, the KV write and
-paged attention through the registered "paged|b200" function, o_proj, a residual
-add, RMSNorm, gate/up projections, SiLU times up, down_proj and a residual add: about
-twenty kernels per layer at a decode batch, most of them small elementwise passes.
-``FusedLlamaDecode`` runs the same step as nine launches per layer:
+A step of ``LlamaForCausalLM`` (transformers models/llama/modeling_llama.py) runs
+each layer as RMSNorm, q/k/v projections, rotary embedding, the KV write and paged
+attention through the registered "paged|b200" function, o_proj, a residual add,
+RMSNorm, gate/up projections, SiLU times up, down_proj and a residual add: about
+twenty kernels per layer, most of them elementwise passes over the step's tokens.
+``FusedLlamaStep`` runs the same step as nine launches per layer:
 
   add_rmsnorm (the previous residual add fused with this layer's input norm),
   one GEMM for q/k/v (the three weights concatenated once at set-up),
   rope_kv_append (rotary embedding of q and k fused with the K/V write to the pool),
-  paged attention (the split-K decode kernel), o_proj,
-  add_rmsnorm, one GEMM for gate/up (concatenated), swiglu, down_proj,
+  paged attention (decode rows on the split-K kernel, prefill rows on tcgen05),
+  o_proj, add_rmsnorm, one GEMM for gate/up (concatenated), swiglu, down_proj,
 
-then the final norm, lm_head on the step's rows and argmax. Rotary embedding is
-bit-identical to HF's; RMSNorm and SiLU * up are computed in fp32 and rounded once,
-where HF rounds an intermediate to the model's dtype first (at most one ulp apart).
-bf16 / fp16 models only.
+then the final norm and lm_head on each row's last token only. Every kernel works
+row by row, so one step may mix prefill chunks and decode rows. Rotary embedding
+is bit-identical to HF's; RMSNorm and SiLU * up are computed in fp32 and rounded
+once, where HF rounds an intermediate to the model's dtype first (at most one ulp
+apart). bf16 / fp16 models only.
 """
 from __future__ import annotations
 
@@ -27,14 +28,14 @@ from . import ops
 from .paged_attention import paged_flash_attention
 
 
-class FusedLlamaDecode:
-    """One decode step (one new token per row) of `model` with fused layer kernels."""
+class FusedLlamaStep:
+    """One step of `model` (prefill chunks and decode rows) with fused layer kernels."""
 
     def __init__(self, model):
         cfg = model.config
         dtype = next(model.parameters()).dtype
         if dtype not in (torch.bfloat16, torch.float16):
-            raise ValueError(f"FusedLlamaDecode: bf16 or fp16 model required, got {dtype}")
+            raise ValueError(f"FusedLlamaStep: bf16 or fp16 model required, got {dtype}")
         inner = model.model
         self.hq = cfg.num_attention_heads
         self.hkv = cfg.num_key_value_heads
@@ -55,9 +56,9 @@ class FusedLlamaDecode:
                 at, mlp = layer.self_attn, layer.mlp
                 lins = (at.q_proj, at.k_proj, at.v_proj, at.o_proj, mlp.gate_proj, mlp.up_proj, mlp.down_proj)
                 if any(lin.bias is not None for lin in lins):
-                    raise ValueError("FusedLlamaDecode: projections with bias are not supported")
+                    raise ValueError("FusedLlamaStep: projections with bias are not supported")
                 if getattr(cfg, "hidden_act", "silu") != "silu":
-                    raise ValueError(f"FusedLlamaDecode: activation {cfg.hidden_act} is not supported (silu)")
+                    raise ValueError(f"FusedLlamaStep: activation {cfg.hidden_act} is not supported (silu)")
                 self.layers.append({
                     "wqkv": torch.cat([at.q_proj.weight, at.k_proj.weight, at.v_proj.weight]).contiguous(),
                     "wo": at.o_proj.weight,
@@ -76,10 +77,12 @@ class FusedLlamaDecode:
 
     @torch.inference_mode()
     def logits(self, tokens: torch.Tensor, positions: torch.Tensor, slots: torch.Tensor, kv_cache: torch.Tensor,
-               metadata: dict) -> torch.Tensor:
-        """tokens, positions, slots: [rows] int64 (one new token per row); kv_cache:
-        [layers, 2, num_blocks, 16, kv heads, head_dim]; metadata: the step's paged
-        metadata (one query per row). Returns the rows' logits [rows, vocab]."""
+               metadata: dict, last: torch.Tensor | None = None) -> torch.Tensor:
+        """tokens, positions, slots: [n_tokens] int64, the step's flattened tokens;
+        kv_cache: [layers, 2, num_blocks, 16, kv heads, head_dim]; metadata: the
+        step's paged metadata; last: the index of each row's last token (default:
+        every token is a row's last, as in a decode step). Returns the logits of
+        those tokens [rows, vocab]."""
         b = tokens.shape[0]
         cos, sin = self.rotary(positions)
         x = torch.index_select(self.embed, 0, tokens)  # residual stream, updated in place
@@ -94,4 +97,6 @@ class FusedLlamaDecode:
             dn = ops.swiglu(h @ w["wgu"].t()) @ w["wd"].t()
             nxt = self.layers[li + 1]["n1"] if li + 1 < len(self.layers) else self.final_norm
             h = ops.add_rmsnorm(x, dn, nxt, self.eps)
+        if last is not None:
+            h = h.index_select(0, last)
         return h @ self.lm_head.t()

@@ -55,7 +55,7 @@ def test_greedy_tokens_match_reference_engine(golden_meta, graphs):
 def run_config4(model, w, graphs=False, record_logits=False, fused=False):
     eng = E2EEngine(model, num_blocks=w["num_gpu_blocks"], max_num_batched_tokens=w["max_num_batched_tokens"],
                     max_num_seqs=w["max_num_seqs"], min_chunk_size=w["min_chunk_size"], use_graphs=graphs,
-                    max_context=512, record_logits=record_logits, fused_decode=fused)
+                    max_context=512, record_logits=record_logits, fused_steps=fused)
     if graphs:
         eng.capture_graphs(buckets=[1, 2, 4, 8, 16])
     last = max(w["arrivals"])
@@ -104,65 +104,78 @@ def test_config4_shape_bf16_divergence_is_near_tie(golden_meta, golden_arrays, c
                                                         for rid, n, ids, vals in eng.logit_log})
 
 
-def test_config4_shape_bf16_fused_graph_decode(golden_meta, golden_arrays, config4_bf16):
-    """Decode steps replayed from graphs of the fused layer kernels
-    (llama_decode.FusedLlamaDecode), prefill steps through the HF modules: the
-    same schedule, and the same near-tie triage against the fp32 reference. The
-    fused path's logits are not recorded, so the triage uses the HF path's
-    logits at the first diverging token; a fused decode divergence that is not a
-    near-tie shows up as tokens leaving the HF bf16 run's far from a tie."""
+def test_config4_shape_bf16_fused_steps(golden_meta, golden_arrays, config4_bf16):
+    """Every step through the fused layer kernels (llama_step.FusedLlamaStep),
+    decode steps replayed from graphs of them: the same schedule, and the same
+    near-tie triage against the fp32 reference as the HF modules' bf16 run."""
     w = e2e_config4_workload()
-    eng = run_config4(config4_bf16, w, graphs=True, fused=True)
-    assert eng.trace == golden_meta["e2e_config4_fp32"]["trace"]
-    assert any(st.kind == "decode" for st in eng.stats)
-    hf = run_config4(config4_bf16, w, record_logits=True)
-    hf_at = {(rid, n): (ids, vals) for rid, n, ids, vals in hf.logit_log}
-    agree = sum(a == b for s, t in zip(eng.seqs, hf.seqs) for a, b in zip(s.out, t.out))
+    eng = run_config4(config4_bf16, w, record_logits=True, fused=True)  # eager steps: logits recorded
+    triage_against_fp32(golden_meta, golden_arrays, eng, {(rid, n): (ids, vals)
+                                                        for rid, n, ids, vals in eng.logit_log})
+    graphs = run_config4(config4_bf16, w, graphs=True, fused=True)
+    assert graphs.trace == golden_meta["e2e_config4_fp32"]["trace"]
+    assert any(st.kind == "decode" for st in graphs.stats)
+    # Graph steps run padded bucket sizes (other GEMM and split choices, other
+    # rounding): where a request's tokens leave the eager fused run's, the graph
+    # token must be a near-tie in the eager run's logits at that point.
+    eager_at = {(rid, n): (ids, vals) for rid, n, ids, vals in eng.logit_log}
+    agree = sum(a == b for s, t in zip(graphs.seqs, eng.seqs) for a, b in zip(s.out, t.out))
     assert agree >= 0.5 * sum(len(s.out) for s in eng.seqs)
-    for s, t in zip(eng.seqs, hf.seqs):
+    for s, t in zip(graphs.seqs, eng.seqs):
         n = next((i for i, (a, b) in enumerate(zip(s.out, t.out)) if a != b), None)
         if n is None:
             continue
-        ids, vals = hf_at[(s.rid, n)]
-        assert s.out[n] in ids, f"request {s.rid}: fused token {s.out[n]} not in the HF top-5 {ids}"
-        margin = vals[0] - vals[ids.index(s.out[n])]
-        assert margin <= 0.1, f"request {s.rid} output {n}: HF margin {margin} is no near-tie"
+        ids, vals = eager_at[(s.rid, n)]
+        assert s.out[n] in ids, f"request {s.rid}: graph token {s.out[n]} not in the eager top-5 {ids}"
+        assert vals[0] - vals[ids.index(s.out[n])] <= 0.1, f"request {s.rid} output {n}: no near-tie"
 
 
-def test_fused_decode_logits_match_hf_modules():
-    """One decode step on the same pool state through the HF modules and through
-    FusedLlamaDecode: the logits agree to bf16 rounding noise."""
-    from serving_engine_b200.llama_decode import FusedLlamaDecode
+def test_fused_step_logits_match_hf_modules():
+    """One mixed step (prefill chunks and decode rows) on the same pool state
+    through the HF modules and through FusedLlamaStep: the last-token logits agree
+    to bf16 rounding noise, both write the step's KV rows alike up to that noise,
+    and the fused step leaves every other slot untouched."""
+    from serving_engine_b200.kv_cache import PagedKVCache, register
+    from serving_engine_b200.llama_step import FusedLlamaStep
     from serving_engine_b200.paged_attention import metadata_from_lists
 
+    register()
     model = random_llama("tiny", seed=4, dtype=torch.bfloat16, device="cuda")
-    eng = E2EEngine(model, num_blocks=128, max_num_batched_tokens=256)
-    for p in config4_requests(seed=5, n=6, vocab=1000):
-        eng.add_request(p[:30 + len(p) % 50], 3)
-    while any(not s.decoding for s in eng.seqs):  # prefill everything
-        eng.step()
-    seqs = [s for s in eng.seqs if s.decoding and s.status == "running"]
-    for s in seqs:
-        eng.pool.grow(s)
-    pos = [s.total_len - 1 for s in seqs]
-    slots = [s.table[p // 16] * 16 + p % 16 for s, p in zip(seqs, pos)]
+    model.set_attn_implementation("paged|b200")
+    cfg = model.config
     dev = torch.device("cuda")
-    ids = torch.tensor([s.out[-1] for s in seqs], device=dev)
-    pos_t = torch.tensor(pos, device=dev)
-    slot_t = torch.tensor(slots, device=dev)
-    md = metadata_from_lists([1] * len(seqs), [p + 1 for p in pos], list(range(len(seqs))), pos,
-                             [s.table for s in seqs], dev)
-    snapshot = eng.kv_cache.clone()
+    gen = torch.Generator().manual_seed(9)
+    rows = [(57, 0), (1, 90), (33, 48), (1, 17), (1, 200)]  # (q_len, num_computed)
+    tables, free = [], list(range(300))
+    for ql, qp in rows:
+        tables.append([free.pop() for _ in range(-(-(ql + qp) // 16))])
+    toks = torch.randint(0, cfg.vocab_size, (sum(r[0] for r in rows),), generator=gen).to(dev)
+    pos = torch.cat([torch.arange(qp, qp + ql) for ql, qp in rows]).to(dev)
+    slots = torch.tensor([tables[i][p // 16] * 16 + p % 16 for i, (ql, qp) in enumerate(rows)
+                          for p in range(qp, qp + ql)], device=dev)
+    q_lens = [r[0] for r in rows]
+    q_starts = np.concatenate(([0], np.cumsum(q_lens)[:-1])).tolist()
+    md = metadata_from_lists(q_lens, [r[0] + r[1] for r in rows], q_starts, [r[1] for r in rows], tables, dev)
+    last = torch.tensor(np.cumsum(q_lens) - 1, device=dev)
+    pool0 = torch.randn(cfg.num_hidden_layers, 2, 300, 16, cfg.num_key_value_heads, cfg.head_dim,
+                        generator=gen).to(torch.bfloat16).to(dev)
+    pool_hf, pool_fu = pool0.clone(), pool0.clone()
     with torch.inference_mode():
-        ref = model(input_ids=ids[None], position_ids=pos_t[None], attention_mask=None, past_key_values=None,
-                    use_cache=False, cache=eng.cache, write_index=slot_t, paged_metadata=md,
-                    logits_to_keep=torch.arange(len(seqs), device=dev)).logits[0].float()
-        eng.kv_cache.copy_(snapshot)
-        fused = FusedLlamaDecode(model).logits(ids, pos_t, slot_t, eng.kv_cache, md).float()
+        ref = model(input_ids=toks[None], position_ids=pos[None], attention_mask=None, past_key_values=None,
+                    use_cache=False, cache=PagedKVCache(pool_hf), write_index=slots, paged_metadata=md,
+                    logits_to_keep=last).logits[0].float()
+        fused = FusedLlamaStep(model).logits(toks, pos, slots, pool_fu, md, last).float()
     check_device_errors()
     cos = torch.nn.functional.cosine_similarity(fused, ref, dim=-1)
     assert float(cos.min()) > 0.9999, cos
     assert float((fused - ref).abs().max()) < 0.02 * float(ref.abs().max())
+    shape = (cfg.num_hidden_layers, 2, -1, cfg.num_key_value_heads, cfg.head_dim)
+    torch.testing.assert_close(pool_fu.view(shape)[:, :, slots].float(), pool_hf.view(shape)[:, :, slots].float(),
+                               atol=0.05, rtol=0.05)
+    untouched = torch.ones(pool0.shape[2] * 16, dtype=torch.bool, device=dev)
+    untouched[slots] = False
+    assert torch.equal(pool_fu.view(shape)[:, :, untouched].view(torch.int16),
+                       pool0.view(shape)[:, :, untouched].view(torch.int16))
 
 
 def triage_against_fp32(golden_meta, golden_arrays, eng, ours_at):
@@ -198,7 +211,8 @@ def triage_against_fp32(golden_meta, golden_arrays, eng, ours_at):
         assert oids[0] in rids_ and rids_[0] in oids, f"not a reordered top-5: {entry}"
         assert ref_margin <= 2 * noise + 1e-6, f"argmax margin beyond the bf16 logit noise: {entry}"
     print("bf16 vs fp32 reference:", report)
-    assert noise < 0.1, f"bf16 logit noise {noise} too large for a bf16 model"
+    scale = float(np.abs(ref_vals[:, 0]).max())  # the reference's largest top-1 logit
+    assert noise < 0.05 * scale, f"bf16 logit noise {noise} beyond 5 % of the logit scale {scale}"
 
 
 def test_bf16_engine_runs_chunked_and_mixed_steps():
