@@ -137,6 +137,78 @@ __device__ __forceinline__ float fast_exp2(float x) {
   return y;
 }
 
+// Packed fp32 pairs (sm_100 f32x2 instructions: one issue slot for the two
+// lanes of an FMA, add, subtract or multiply), so that the softmax, which is
+// bound by issue slots and the MUFU, spends half the slots on its fp32 work.
+__device__ __forceinline__ uint64_t f2_pack(float2 v) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(v.x), "f"(v.y));
+  return r;
+}
+__device__ __forceinline__ float2 f2_unpack(uint64_t v) {
+  float2 r;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(r.x), "=f"(r.y) : "l"(v));
+  return r;
+}
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(f2_pack(a)), "l"(f2_pack(b)), "l"(f2_pack(c)));
+  return f2_unpack(d);
+}
+__device__ __forceinline__ float2 add2(float2 a, float2 b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(f2_pack(a)), "l"(f2_pack(b)));
+  return f2_unpack(d);
+}
+__device__ __forceinline__ float2 sub2(float2 a, float2 b) {
+  uint64_t d;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(f2_pack(a)), "l"(f2_pack(b)));
+  return f2_unpack(d);
+}
+__device__ __forceinline__ float2 mul2(float2 a, float2 b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(f2_pack(a)), "l"(f2_pack(b)));
+  return f2_unpack(d);
+}
+__device__ __forceinline__ float2 splat2(float v) { return make_float2(v, v); }
+
+// max(a, b, c) in one instruction (sm_100); NaN operands are dropped as fmaxf drops them.
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
+// 2^x for two scores on the FMA pipe, so that part of a tile's exponentials
+// run beside the MUFU's. Cody-Waite range reduction: 2^x = 2^j * 2^f with
+// j = rint(x) (the 1.5 * 2^23 addition leaves j in the low mantissa bits) and
+// f = x - j in [-1/2, 1/2], exact; 2^f by the degree-3 polynomial that minimises
+// the relative error on that interval (coefficients fitted for this kernel by a
+// linear program: 7.5e-5 relative error in fp32, against 2^-9 for the 16-bit P
+// it feeds). Valid for x <= 127. It is used only on unmasked tiles (no -inf
+// scores); there a score more than 126 below the row's reference maximum weighs
+// about 1.2e-38 instead of ex2's 0. max.NaN keeps a NaN score NaN, as ex2 does.
+__device__ __forceinline__ float2 poly_exp2x2(float2 x) {
+  asm("max.NaN.f32 %0, %0, 0fC2FC0000;" : "+f"(x.x));  // max(x, -126)
+  asm("max.NaN.f32 %0, %0, 0fC2FC0000;" : "+f"(x.y));
+  const float2 t = add2(x, splat2(12582912.f));
+  const float2 f = sub2(x, sub2(t, splat2(12582912.f)));
+  float2 p = fma2(splat2(0x1.c3f76p-5f), f, splat2(0x1.f0de1ap-3f));
+  p = fma2(p, f, splat2(0x1.62f31ap-1f));
+  p = fma2(p, f, splat2(0x1.fff692p-1f));
+  const float2 scale = make_float2(__int_as_float((__float_as_int(t.x) << 23) + 0x3f800000),
+                                   __int_as_float((__float_as_int(t.y) << 23) + 0x3f800000));  // 2^j
+  return mul2(p, scale);
+}
+
+// Pairs of a 32-score chunk (bit e: scores 2e, 2e + 1) whose exponentials the
+// pair kernel evaluates with poly_exp2 on unmasked tiles of pairs without the
+// remainder pass.
+#ifndef SEB_POLY_PAIRS
+#define SEB_POLY_PAIRS 0x8888u
+#endif
+constexpr unsigned kPolyPairs = SEB_POLY_PAIRS;
+
 __device__ __forceinline__ bool wait_or_flag(uint32_t bar, uint32_t parity, bool& failed) {
   if (failed) return false;
   if (!mbar_wait_bounded(bar, parity)) {
@@ -169,6 +241,15 @@ __device__ __forceinline__ void mask_chunk(float (&x)[32], int key0, int vis, in
     else if (key >= k_len) v = 0.f;
     x[i] = v;
   }
+}
+
+// Causal masking of raw (unscaled) scores of a row whose visible keys all lie
+// below k_len: keys at or past the row's visible end -> -inf. The positive
+// scale is applied afterwards (-inf stays -inf), one compare and select a score.
+__device__ __forceinline__ void mask_chunk_causal(float (&x)[32], int key0, int vis) {
+  const int lim = vis - key0;
+#pragma unroll
+  for (int i = 0; i < 32; ++i) x[i] = i < lim ? x[i] : -INFINITY;
 }
 
 template <typename T, int D>
@@ -459,8 +540,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       wait_or_flag(bar + 8 * (kBarSFull + qt), j & 1, failed);
       tc::fence_after_sync();
       // Tiles every valid row of the Q tile sees in full need no mask: scores
-      // stay raw and the scale folds into the exponent's FMA.
-      const bool full = (j + 1) * kBN <= min_vis && (j + 1) * kBN <= k_len;
+      // stay raw and the (positive) scale folds into the row max and the
+      // exponent's FMA. Any other scale takes the masked path, which scales first.
+      const bool full = c > 0.f && (j + 1) * kBN <= min_vis && (j + 1) * kBN <= k_len;
       const float cm = full ? c : 1.f;
       // The row's 128 scores in one TMEM round trip.
       float x[4][32];
@@ -615,7 +697,8 @@ struct PairLayout {
   static constexpr int oQ = 0;                 // [2 buffers]
   static constexpr int oK = oQ + 2 * kTileQ;
   static constexpr int oV = oK + kPairKStages * kStageK;
-  static constexpr int oBar = oV + kPairVStages * kStageV;
+  static constexpr int oO = oV + kPairVStages * kStageV;  // O staged for its TMA store: one panel per half
+  static constexpr int oBar = oO + kTileQ;
   static constexpr int oX = oBar + 512;        // [tile parity][half][row] row maxima; row sums at unit ends
   static constexpr int kBytes = oX + 2 * 2 * 128 * 4;
 };
@@ -677,7 +760,8 @@ __device__ __forceinline__ bool pair_unit(const PrefillParams& p, int u, PairUni
 template <typename T>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
     prefill_pair_kernel(const PrefillParams p, const __grid_constant__ CUtensorMap tmap_q,
-                        const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ CUtensorMap tmap_v) {
+                        const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ CUtensorMap tmap_v,
+                        const __grid_constant__ CUtensorMap tmap_o) {
   using L = PairLayout;
   constexpr int D = 128;
   constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
@@ -955,6 +1039,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
       }
       const int vis = row_valid ? (p.causal ? min(w.ceil16, w.qpos0 + qi + 1) : w.ceil16) : 0;
       const int min_vis = p.causal ? min(w.ceil16, w.qpos0 + i0 + 1) : w.ceil16;
+      // Scores stay raw (the scale folds into the row max and the exponent's
+      // FMA) on unmasked tiles and, for causal rows that see no key past k_len,
+      // on masked ones too; that needs a positive scale.
+      const bool pos_scale = c > 0.f;
+      const bool causal_raw = pos_scale && p.causal && w.qpos0 + w.q_len <= w.k_len;
       float m_ref = -INFINITY;
       float l = 0.f;
       for (int j = 0; j < w.ntiles; ++j, ++g) {
@@ -962,23 +1051,28 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
         const uint32_t col_s = 128 * b;
         wait_or_flag_cluster(bar + 8 * (kPBarSFull + b), (g / 3) & 1, failed);
         tc::fence_after_sync();
-        const bool full = (j + 1) * kBN <= min_vis && (j + 1) * kBN <= w.k_len;
-        const float cm = full ? c : 1.f;
+        const bool full = pos_scale && (j + 1) * kBN <= min_vis && (j + 1) * kBN <= w.k_len;
+        const bool raw = full || causal_raw;
+        const float cm = raw ? c : 1.f;
         float x[2][32];
 #pragma unroll
         for (int ch = 0; ch < 2; ++ch) tc::tmem_ld32(taddr + col_s + kh0 + 32 * ch, x[ch]);
         tc::tmem_wait_ld();
         if (!full) {
+          if (raw) {
 #pragma unroll
-          for (int ch = 0; ch < 2; ++ch) mask_chunk(x[ch], j * kBN + kh0 + 32 * ch, vis, w.k_len, c);
+            for (int ch = 0; ch < 2; ++ch) mask_chunk_causal(x[ch], j * kBN + kh0 + 32 * ch, vis);
+          } else {
+#pragma unroll
+            for (int ch = 0; ch < 2; ++ch) mask_chunk(x[ch], j * kBN + kh0 + 32 * ch, vis, w.k_len, c);
+          }
         }
         float mx[8];
 #pragma unroll
         for (int i = 0; i < 8; ++i)
-          mx[i] = fmaxf(fmaxf(fmaxf(x[0][i], x[0][8 + i]), fmaxf(x[0][16 + i], x[0][24 + i])),
-                        fmaxf(fmaxf(x[1][i], x[1][8 + i]), fmaxf(x[1][16 + i], x[1][24 + i])));
-        const float mh = cm * fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
-                                    fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
+          mx[i] = fmax3(fmax3(x[0][i], x[0][8 + i], x[0][16 + i]), fmax3(x[0][24 + i], x[1][i], x[1][8 + i]),
+                        fmaxf(x[1][16 + i], x[1][24 + i]));
+        const float mh = cm * fmax3(fmax3(mx[0], mx[1], mx[2]), fmax3(mx[3], mx[4], mx[5]), fmaxf(mx[6], mx[7]));
         // Row max over both halves. The barrier also orders both halves' S loads
         // before either half's P stores (P of keys 64-127 lands on S columns of
         // keys 32-63, the remainder on those of keys 64-127).
@@ -996,33 +1090,45 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
           m_ref = mb;
         }
         const float neg_m = m_ref == -INFINITY ? 0.f : -m_ref;
-        float ls[4] = {0.f, 0.f, 0.f, 0.f};
+        float2 ls[4] = {splat2(0.f), splat2(0.f), splat2(0.f), splat2(0.f)};
+        // P of the tile's 64 scores of this row: exponentials, row sum, 16-bit
+        // P into the S buffer (and its remainder for split pairs). Unmasked
+        // tiles of unsplit pairs take kPolyPairs' share on the FMA pipe.
+        auto exponentiate = [&](auto poly_tag) {
+          constexpr bool kPoly = decltype(poly_tag)::value;
+          const float2 cm2 = splat2(cm), nm2 = splat2(neg_m);
 #pragma unroll
-        for (int ch = 0; ch < 2; ++ch) {
-          {
-            uint32_t hi[16];
+          for (int ch = 0; ch < 2; ++ch) {
+            {
+              uint32_t hi[16];
 #pragma unroll
-            for (int e = 0; e < 16; ++e) {
-              const float a0 = fast_exp2(fmaf(x[ch][2 * e], cm, neg_m));
-              const float a1 = fast_exp2(fmaf(x[ch][2 * e + 1], cm, neg_m));
-              ls[e & 3] += a0 + a1;
-              hi[e] = Mma<T>::pack(a0, a1);
-              x[ch][2 * e] = a0;
-              x[ch][2 * e + 1] = a1;
+              for (int e = 0; e < 16; ++e) {
+                const float2 y = fma2(make_float2(x[ch][2 * e], x[ch][2 * e + 1]), cm2, nm2);
+                float2 a;
+                if (kPoly && ((kPolyPairs >> e) & 1u)) a = poly_exp2x2(y);
+                else a = make_float2(fast_exp2(y.x), fast_exp2(y.y));
+                ls[e & 3] = add2(ls[e & 3], a);
+                hi[e] = Mma<T>::pack(a.x, a.y);
+                x[ch][2 * e] = a.x;
+                x[ch][2 * e + 1] = a.y;
+              }
+              tc::tmem_st16u(taddr + col_s + kh0 / 2 + 16 * ch, hi);
             }
-            tc::tmem_st16u(taddr + col_s + kh0 / 2 + 16 * ch, hi);
-          }
-          if (w.split) {
-            uint32_t lo[16];
+            if (!kPoly && w.split) {
+              uint32_t lo[16];
 #pragma unroll
-            for (int e = 0; e < 16; ++e) {
-              const float2 f = Mma<T>::unpack(Mma<T>::pack(x[ch][2 * e], x[ch][2 * e + 1]));
-              lo[e] = Mma<T>::pack(x[ch][2 * e] - f.x, x[ch][2 * e + 1] - f.y);
+              for (int e = 0; e < 16; ++e) {
+                const float2 f = Mma<T>::unpack(Mma<T>::pack(x[ch][2 * e], x[ch][2 * e + 1]));
+                lo[e] = Mma<T>::pack(x[ch][2 * e] - f.x, x[ch][2 * e + 1] - f.y);
+              }
+              tc::tmem_st16u(taddr + col_s + 64 + kh0 / 2 + 16 * ch, lo);
             }
-            tc::tmem_st16u(taddr + col_s + 64 + kh0 / 2 + 16 * ch, lo);
           }
-        }
-        l += (ls[0] + ls[1]) + (ls[2] + ls[3]);
+        };
+        if (kPolyPairs != 0u && full && !w.split) exponentiate(std::true_type{});
+        else exponentiate(std::false_type{});
+        const float2 ls2 = add2(add2(ls[0], ls[1]), add2(ls[2], ls[3]));
+        l += ls2.x + ls2.y;
         if (j > 0 && __any_sync(kFullMask, need)) {
           // O must hold P V(j - 1) before it is rescaled; each half scales its 64 dims
           const int gp = g - 1;
@@ -1059,8 +1165,41 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
       const int gl = g - 1;
       wait_or_flag_cluster(bar + 8 * (kPBarPFree + gl % 3), (gl / 3) & 1, failed);
       tc::fence_after_sync();
-      if (!__any_sync(kFullMask, failed)) {
-        const float inv = 1.f / l;
+      const bool ok = !__any_sync(kFullMask, failed);
+      const float inv = 1.f / l;
+      if (i0 + p.qpt <= w.q_len) {
+        // Every row of the tile is a query of this row: O goes through shared
+        // memory, each thread's 64 values as one 128-byte row of its half's
+        // panel (128B-swizzled, as the output map expects), and out in one TMA
+        // store per half instead of 32 scattered rows per warp instruction.
+        const bool issuer = (warp & 3) == 2 && lane == 0;  // warps 2 and 6
+        if (issuer) bulk_wait_read_all();                  // the previous unit's store has read the panel
+        named_bar_sync(5 + khalf, 128);
+        char* panel = sbase + L::oO + khalf * L::kPanelQ;
+        if (ok) {
+#pragma unroll
+          for (int cc = 0; cc < 2; ++cc) {
+            float o[32];
+            tc::tmem_ld32(taddr + kPairColO + kh0 + 32 * cc, o);
+            tc::tmem_wait_ld();
+#pragma unroll
+            for (int v8 = 0; v8 < 4; ++v8) {
+              uint32_t wv[4];
+#pragma unroll
+              for (int e = 0; e < 4; ++e)
+                wv[e] = Mma<T>::pack(o[8 * v8 + 2 * e] * inv, o[8 * v8 + 2 * e + 1] * inv);
+              const int chunk = (4 * cc + v8) ^ (m & 7);
+              *reinterpret_cast<uint4*>(panel + m * 128 + chunk * 16) = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+            }
+          }
+        }
+        fence_proxy_async_smem();
+        named_bar_sync(5 + khalf, 128);
+        if (issuer && ok) {
+          tma_store_3d(&tmap_o, smem_u32(panel), kh0, w.kvh * G, w.q_start + i0);
+          bulk_commit_group();
+        }
+      } else if (ok) {
 #pragma unroll
         for (int cc = 0; cc < 2; ++cc) {
           float o[32];
@@ -1077,12 +1216,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
             }
           }
         }
-        if (row_valid && khalf == 0) *lp = m_ref * kLn2p + logf(l);
       }
+      if (ok && row_valid && khalf == 0) *lp = m_ref * kLn2p + logf(l);
       // The next unit's first P V overwrites O: order this warp's O loads before
       // its next P arrival.
       tc::fence_before_sync();
     }
+    if ((warp & 3) == 2 && lane == 0) bulk_wait_all();  // O stores complete before the CTA exits
   }
 
   if (failed && lane == 0) atomic_or_err(p.err, SEB_ERRBIT_TIMEOUT);
@@ -1112,10 +1252,15 @@ int launch_prefill_pair(const PrefillParams& p, const void* q, int64_t q_st, int
   if (rc != SEB_OK) return rc;
   rc = kv_tensor_map(&tv, vc, dtype, p.num_blocks, p.hkv, 128);
   if (rc != SEB_OK) return rc;
+  // O of a whole Q tile, stored as Q was loaded: (64 dims, group heads, qpt queries) boxes
+  CUtensorMap to;
+  const uint64_t ostr[2] = {(uint64_t)p.o_sh * 2, (uint64_t)p.o_st * 2};
+  rc = tensor_map_3d(&to, p.out, dtype, qdims, ostr, qbox);
+  if (rc != SEB_OK) return rc;
   // persistent: one cluster per pair of SMs (or per unit, when there are fewer)
   const int64_t units = p.unit_list ? (int64_t)p.unit_cap : (int64_t)p.num_prefill_rows * p.hkv * p.mpairs;
   const int64_t clusters = std::min<int64_t>(units, num_sms() / 2);
-  kern<<<(unsigned)(2 * clusters), kPairThreads, smem, s>>>(p, tq, tk, tv);
+  kern<<<(unsigned)(2 * clusters), kPairThreads, smem, s>>>(p, tq, tk, tv, to);
   return launch_status("prefill_pair_kernel");
 }
 

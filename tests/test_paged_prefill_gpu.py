@@ -102,6 +102,54 @@ def test_prefill_long_chunk_shared_prefix():
     assert_close(o, lse, o_ref, lse_ref, torch.bfloat16)
 
 
+@pytest.mark.parametrize("hq,hkv", [(32, 8), (8, 8), (32, 4), (16, 1)])
+def test_prefill_long_context_rows(hq, hkv):
+    """Pairs whose first query sees at least 1,024 keys skip P's remainder pass;
+    on their unmasked tiles part of the exponentials is a polynomial on the FMA
+    pipe instead of the MUFU's ex2. Ragged tails, partial last blocks and a
+    row that crosses from split pairs to unsplit ones meet the same bound, the
+    plain 2e-3 where it applies included."""
+    rows = [(96, 1100), (130, 2047), (33, 1500), (200, 900)]
+    b = make_batch(rows, hq, hkv, 128, torch.bfloat16, seed=41 + hq + hkv)
+    o, lse = run_prefill(b)
+    o_ref, lse_ref = oracle(b)
+    strict = strict_mask(o_ref, torch.bfloat16)
+    worst = float(np.abs(o - o_ref)[strict].max())
+    assert worst <= 2e-3, f"strict band max error {worst:.3g}; bands {band_report(o, o_ref)}"
+    assert_close(o, lse, o_ref, lse_ref, torch.bfloat16)
+
+
+@pytest.mark.parametrize("d", [64, 128])
+def test_prefill_nan_key_poisons_the_rows_that_see_it(d):
+    """A NaN in a visible key makes every output (and LSE) of the query heads
+    that see it NaN, as the reference's exp of a NaN score does, whichever way
+    the exponential was evaluated; queries that do not see it, other kv heads
+    and other rows stay finite and match the oracle."""
+    rows = [(64, 1200), (40, 1300), (80, 600)]
+    b = make_batch(rows, 32, 8, d, torch.bfloat16, seed=31 + d)
+    key = 1210  # inside row 0's chunk: its first 10 queries do not see it
+    b.k_cache[b.block_tables[0][key // 16], key % 16, 3, 5] = float("nan")
+    o, lse = run_prefill(b)
+    o_ref, lse_ref = oracle(b)
+    assert np.isnan(o_ref[10:64, 12:16]).all() and not np.isnan(o_ref[:10]).any()
+    assert not np.isnan(np.delete(o_ref[:64], range(12, 16), axis=1)).any() and not np.isnan(o_ref[64:]).any()
+    assert_close(o, lse, o_ref, lse_ref, torch.bfloat16)
+
+
+@pytest.mark.parametrize("d", [64, 128])
+@pytest.mark.parametrize("scale_mul", [-1.0, 0.0, 0.5])
+def test_prefill_any_scale(d, scale_mul):
+    """The kernels fold a positive scale into the row max and the exponent;
+    a negative or zero scale (legal for the reference, which just multiplies)
+    takes the path that scales scores first, and still matches the oracle."""
+    rows = [(70, 1100), (33, 0), (130, 200)]
+    b = make_batch(rows, 32, 8, d, torch.bfloat16, seed=53 + d)
+    b.scale = scale_mul / math.sqrt(d)
+    o, lse = run_prefill(b)
+    o_ref, lse_ref = oracle(b)
+    assert_close(o, lse, o_ref, lse_ref, torch.bfloat16)
+
+
 def test_prefill_noncausal_and_partial_blocks():
     rows = [(40, 0), (17, 9), (64, 63)]
     b = make_batch(rows, 16, 4, 128, torch.bfloat16, seed=7)
