@@ -128,6 +128,18 @@ __device__ __forceinline__ ItemInfo item_info(const DecodeParams& p, int item) {
   return it;
 }
 
+// Work unit of global warp w: the kv head varies fastest, then the split, then
+// the item. The warps of one CTA thus share an (item, split) and are live or
+// idle together (a split past the row's length exits at once), so a CTA never
+// holds its shared-memory ring for one working warp while its others idle; and
+// they read the same block ids, whose kv-head tiles are neighbours in the pool.
+__device__ __forceinline__ int64_t unit_of_warp(const DecodeParams& p, int64_t w, int& kvh, int& split) {
+  kvh = (int)(w % p.hkv);
+  const int64_t tmp = w / p.hkv;
+  split = (int)(tmp % p.max_splits);
+  return tmp / p.max_splits;
+}
+
 __device__ __forceinline__ void report_item(const DecodeParams& p, const ItemInfo& it, int lane) {
   if (lane != 0) return;
   if (!it.ok) atomic_or_err(p.err, SEB_ERRBIT_META);
@@ -299,11 +311,8 @@ __global__ void __launch_bounds__(WARPS * 32)
   const int g = lane >> 2;
   const int t = lane & 3;
 
-  const int64_t w = (int64_t)blockIdx.x * WARPS + warp;
-  const int split = (int)(w % p.max_splits);
-  const int64_t tmp = w / p.max_splits;
-  const int kvh = (int)(tmp % p.hkv);
-  const int64_t item = tmp / p.hkv;
+  int kvh, split;
+  const int64_t item = unit_of_warp(p, (int64_t)blockIdx.x * WARPS + warp, kvh, split);
   if (item >= p.num_items || (p.num_items_dev && item >= __ldg(p.num_items_dev))) return;
 
   const ItemInfo it = item_info(p, (int)item);
@@ -599,11 +608,8 @@ __global__ void __launch_bounds__(WARPS * 32) decode_simt_kernel(const DecodePar
   constexpr int DL = D / 32;
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int64_t w = (int64_t)blockIdx.x * WARPS + warp;
-  const int split = (int)(w % p.max_splits);
-  const int64_t tmp = w / p.max_splits;
-  const int kvh = (int)(tmp % p.hkv);
-  const int64_t item = tmp / p.hkv;
+  int kvh, split;
+  const int64_t item = unit_of_warp(p, (int64_t)blockIdx.x * WARPS + warp, kvh, split);
   if (item >= p.num_items || (p.num_items_dev && item >= __ldg(p.num_items_dev))) return;
   const ItemInfo it = item_info(p, (int)item);
   if (split == 0 && kvh == 0) report_item(p, it, lane);

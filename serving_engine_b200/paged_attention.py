@@ -165,7 +165,8 @@ class DecodeMetadataBuffer:
     block-table width `width`, resident in one device buffer whose address never
     changes (what a captured CUDA graph reads). Layout as PackedMetadata with
     q_len = 1 for every row: q_lens | k_lens | q_starts | q_pos_offsets |
-    block_table | item_row | decode tokens | decode rows (no prefill rows)."""
+    block_table | item_row | decode tokens | decode rows (no prefill rows); each
+    update lists the decode items longest context first."""
 
     def __init__(self, rows: int, width: int, device):
         self.rows, self.width = rows, width
@@ -210,6 +211,12 @@ class DecodeMetadataBuffer:
         a[r:2 * r] = k_lens
         a[3 * r:4 * r] = k_lens - 1
         a[4 * r:4 * r + r * w] = tables.reshape(-1)
+        # decode items longest context first, as PackedMetadata orders them: the
+        # kernel dispatches work in item order, so the short items fill its tail
+        order = np.argsort(-np.asarray(k_lens, dtype=np.int64), kind="stable").astype(np.int32)
+        o = 4 * r + r * w
+        a[o + r:o + 2 * r] = order
+        a[o + 2 * r:o + 3 * r] = order
         self.dev.copy_(self.host, non_blocking=True)
         ev = torch.cuda.Event()
         ev.record()
