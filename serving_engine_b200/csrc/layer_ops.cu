@@ -122,6 +122,66 @@ __global__ void __launch_bounds__(256) rope_append_kernel(RopeParams p) {
   }
 }
 
+// rope_append_kernel with 16-byte accesses (every row and table 16-byte aligned,
+// head_dim % 16 == 0): one thread per (token, 8-element chunk). A q or k row is
+// head_dim / 16 threads, each rotating elements [i, i + 8) with [i + half,
+// i + half + 8); a v row is head_dim / 8 threads, each copying one chunk. The
+// per-element arithmetic is the one of rope_append_kernel, so both give the
+// same bits; a token's hundreds of threads keep all of its loads in flight at
+// once, where one warp per row left half its lanes idle at head_dim 64.
+template <typename T>
+__global__ void __launch_bounds__(256) rope_append_vec_kernel(RopeParams p) {
+  const int ch = p.d >> 4;  // chunks in half a row
+  const int rot_threads = (p.hq + p.hkv) * ch;
+  const int per_token = rot_threads + p.hkv * 2 * ch;
+  const int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t t = g / per_token;
+  if (t >= p.n_tokens) return;
+  const int rem = (int)(g - t * per_token);
+  const T* src_tok = reinterpret_cast<const T*>(p.qkv + t * p.qkv_st);
+  if (rem >= rot_threads) {  // v: copy one chunk into the token's slot
+    const int r2 = rem - rot_threads;
+    const int h = r2 / (2 * ch), c = r2 - h * 2 * ch;
+    const int64_t slot = __ldg(p.slots + t);
+    if (slot < 0 || slot >= p.num_slots) return;  // reported by the k rows
+    const uint4 v = *reinterpret_cast<const uint4*>(src_tok + (int64_t)(p.hq + p.hkv + h) * p.d + 8 * c);
+    *reinterpret_cast<uint4*>(reinterpret_cast<T*>(p.v_cache) + (slot * p.hkv + h) * p.d + 8 * c) = v;
+    return;
+  }
+  const int r = rem / ch, c = rem - r * ch;
+  const int half = p.d >> 1;
+  const int i = 8 * c;
+  T* dst;
+  if (r < p.hq) {
+    dst = reinterpret_cast<T*>(p.q_out + t * p.q_st) + (int64_t)r * p.d;
+  } else {
+    const int64_t slot = __ldg(p.slots + t);
+    if (slot < 0 || slot >= p.num_slots) {
+      if (r == p.hq && c == 0) atomic_or_err(p.err, SEB_ERRBIT_SLOT);
+      return;
+    }
+    dst = reinterpret_cast<T*>(p.k_cache) + (slot * p.hkv + (r - p.hq)) * p.d;
+  }
+  const T* src = src_tok + (int64_t)r * p.d;
+  const T* cs = reinterpret_cast<const T*>(p.cos + t * p.cs_st);
+  const T* sn = reinterpret_cast<const T*>(p.sin + t * p.cs_st);
+  Vec8<T> x1, x2, c1, c2, s1, s2, lo, hi;
+  x1.raw = *reinterpret_cast<const uint4*>(src + i);
+  x2.raw = *reinterpret_cast<const uint4*>(src + i + half);
+  c1.raw = __ldg(reinterpret_cast<const uint4*>(cs + i));
+  c2.raw = __ldg(reinterpret_cast<const uint4*>(cs + i + half));
+  s1.raw = __ldg(reinterpret_cast<const uint4*>(sn + i));
+  s2.raw = __ldg(reinterpret_cast<const uint4*>(sn + i + half));
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    const float a = x1.get(e), b = x2.get(e);
+    lo.set(e, round_to<T>(a * c1.get(e)) + round_to<T>(-b * s1.get(e)));
+    hi.set(e, round_to<T>(b * c2.get(e)) + round_to<T>(a * s2.get(e)));
+  }
+  *reinterpret_cast<uint4*>(dst + i) = lo.raw;
+  *reinterpret_cast<uint4*>(dst + i + half) = hi.raw;
+}
+
 // One CTA per row: x <- round(x + a) (when a is given), out = x * rsqrt(mean(x^2) + eps) * w.
 template <typename T, int THREADS>
 __global__ void __launch_bounds__(THREADS) add_rmsnorm_kernel(T* x, int64_t x_st, const T* a, int64_t a_st,
@@ -286,10 +346,23 @@ extern "C" int seb_rope_kv_append(const void* qkv, int64_t qkv_stride_token, int
   p.pairs = head_dim % 4 == 0 && aligned(qkv, 4) && aligned(cos, 4) && aligned(sin, 4) && aligned(q_out, 4) &&
             aligned(k_cache, 4) && aligned(v_cache, 4) && qkv_stride_token % 2 == 0 && cos_sin_stride_token % 2 == 0 &&
             q_out_stride_token % 2 == 0;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const bool vec16 = head_dim % 16 == 0 && aligned(qkv, 16) && aligned(cos, 16) && aligned(sin, 16) &&
+                     aligned(q_out, 16) && aligned(k_cache, 16) && aligned(v_cache, 16) &&
+                     qkv_stride_token % 8 == 0 && cos_sin_stride_token % 8 == 0 && q_out_stride_token % 8 == 0;
+  if (vec16) {
+    const int64_t threads = n_tokens * (int64_t)(num_q_heads + 3 * num_kv_heads) * (head_dim / 16);
+    const int64_t blocks = (threads + 255) / 256;
+    SEB_CHECK_ARG(blocks < (1ll << 31), "seb_rope_kv_append: too many tokens");
+    if (dtype == SEB_BF16)
+      rope_append_vec_kernel<__nv_bfloat16><<<(unsigned)blocks, 256, 0, s>>>(p);
+    else
+      rope_append_vec_kernel<__half><<<(unsigned)blocks, 256, 0, s>>>(p);
+    return launch_status("rope_append_vec_kernel");
+  }
   const int64_t warps = n_tokens * (num_q_heads + 2 * num_kv_heads);
   const int64_t blocks = (warps + 7) / 8;
   SEB_CHECK_ARG(blocks < (1ll << 31), "seb_rope_kv_append: too many tokens");
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (dtype == SEB_BF16)
     rope_append_kernel<__nv_bfloat16><<<(unsigned)blocks, 256, 0, s>>>(p);
   else

@@ -30,13 +30,18 @@ def rope_tables(pos, d, dtype):
 
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
-@pytest.mark.parametrize("hq,hkv,d", [(32, 8, 128), (8, 8, 64), (16, 2, 128)])
-@pytest.mark.parametrize("offset", [0, 1])  # 1: a 2-byte-offset view takes the element-at-a-time path
+@pytest.mark.parametrize("hq,hkv,d", [(32, 8, 128), (8, 8, 64), (16, 2, 128), (32, 8, 64)])
+# 0: contiguous rows take the 16-byte-vector kernel; 2: a row stride of w + 2
+# elements the element-pair path; 1: a 2-byte-offset view the element-at-a-time path
+@pytest.mark.parametrize("offset", [0, 2, 1])
 def test_rope_kv_append_bit_exact(dtype, hq, hkv, d, offset):
     g = torch.Generator(device=DEV).manual_seed(hq * d + offset)
     n, nb = 37, 20
     w = (hq + 2 * hkv) * d
-    qkv = torch.randn(n, w + 2, generator=g, device=DEV).to(dtype)[:, offset:offset + w]
+    if offset == 0:
+        qkv = torch.randn(n, w, generator=g, device=DEV).to(dtype)
+    else:
+        qkv = torch.randn(n, w + 2, generator=g, device=DEV).to(dtype)[:, offset % 2:offset % 2 + w]
     pos = torch.randint(0, 4000, (n,), generator=g, device=DEV)
     cos, sin = rope_tables(pos, d, dtype)
     slots = torch.randperm(nb * 16, generator=g, device=DEV)[:n]
@@ -56,9 +61,10 @@ def test_rope_kv_append_bit_exact(dtype, hq, hkv, d, offset):
     assert torch.equal(vc, vc_ref)
 
 
-def test_rope_kv_append_bad_slot_sets_error_and_skips():
+@pytest.mark.parametrize("pad", [0, 2])  # 0: the 16-byte-vector kernel; 2: the warp-per-row kernel
+def test_rope_kv_append_bad_slot_sets_error_and_skips(pad):
     hq, hkv, d, nb = 4, 2, 64, 4
-    qkv = torch.randn(3, (hq + 2 * hkv) * d, device=DEV).to(torch.bfloat16)
+    qkv = torch.randn(3, (hq + 2 * hkv) * d + pad, device=DEV).to(torch.bfloat16)[:, :(hq + 2 * hkv) * d]
     cos, sin = rope_tables(torch.tensor([1, 2, 3], device=DEV), d, torch.bfloat16)
     kc = torch.zeros(nb, 16, hkv, d, device=DEV, dtype=torch.bfloat16)
     vc = torch.zeros_like(kc)
