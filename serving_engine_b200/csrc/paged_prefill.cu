@@ -20,8 +20,9 @@
 //   warp 0     TMA producer: the Q tiles once, then K and V tiles (block ids
 //              prefetched a window ahead) into 2-stage rings;
 //   warp 1     owns TMEM (512 columns: per Q tile, S of 128 columns with P
-//              written over its first 64 as 16-bit pairs, and O) and issues the
-//              MMAs from one thread in ping-pong order: per KV tile j and Q tile
+//              written over its first 64 as 16-bit pairs, O of 64 columns and
+//              64 columns for P's remainder) and issues the MMAs from one
+//              thread in ping-pong order: per KV tile j and Q tile
 //              t, O(t) += P(t, j) V(j) (P read from TMEM), then S(t, j + 1),
 //              so one Q tile's softmax runs while the other's MMAs execute;
 //   warps 2-9  one softmax warpgroup per Q tile; a thread owns one tile row
@@ -56,10 +57,12 @@ constexpr int kThreads = 320;  // producer, MMA, one softmax warpgroup per Q til
 constexpr int kKStages = 2;    // K ring depth
 constexpr int kVStages = 2;    // V ring depth
 constexpr int kTmemCols = 512;
-// TMEM columns of Q tile t: S at t * 128 (128 fp32 scores per row; P overwrites
-// its first 64 columns as packed 16-bit pairs), O at 256 + t * 128.
+// TMEM columns of Q tile t (head_dim 64): S at t * 128 (128 fp32 scores per row;
+// P overwrites its first 64 columns as packed 16-bit pairs), O at 256 + t * 64,
+// P's 16-bit remainder (pairs whose first query sees few keys) at 384 + t * 64.
 constexpr int kColS = 0;
 constexpr int kColO = 256;
+constexpr int kColRem = 384;
 constexpr float kLazyThreshold = 8.0f;
 // One 16-bit rounding of P costs up to about 0.013 / sqrt(visible keys) of
 // output error (8e-4 at 260 keys, 4e-4 at 1000), which next to the output's own
@@ -265,14 +268,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
 
-  // ---- work unit: (prefill row, kv head, pair of Q tiles, half). Pairs are
-  // visited late-first (they are the longest). Half 0 runs both Q tiles of the
-  // pair; a pair whose first query sees fewer than kSplitBelow keys needs P's
-  // remainder and runs one Q tile per CTA instead: half 0 the first, half 1 the
-  // second. Half-1 CTAs of other pairs exit at once.
+  static_assert(D == 64, "TMEM layout for head_dim 64 (O and P's remainder: 64 columns per Q tile)");
+  // ---- work unit: (prefill row, kv head, pair of Q tiles), both Q tiles in
+  // this CTA. Pairs are visited late-first (they are the longest).
   int bx = blockIdx.x;
-  const int half = bx & 1;
-  bx >>= 1;
   int pr, kvh, row;
   if (p.unit_list) {
     if (bx >= __ldg(p.num_units)) return;
@@ -289,7 +288,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (prow >= p.num_prefill_rows) return;
     row = p.rows ? __ldg(p.rows + prow) : prow;
     if (row < 0 || row >= p.num_rows) {
-      if (threadIdx.x == 0 && kvh == 0 && pr == 0 && half == 0) atomic_or_err(p.err, SEB_ERRBIT_META);
+      if (threadIdx.x == 0 && kvh == 0 && pr == 0) atomic_or_err(p.err, SEB_ERRBIT_META);
       return;
     }
   }
@@ -301,10 +300,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int pair0 = pr * kQT * p.qpt;  // first query of the pair
   if (pair0 >= q_len) return;
   const bool has_second = pair0 + p.qpt < q_len;
-  const bool pair_split = (p.causal ? min(ceil16, qpos0 + pair0 + 1) : ceil16) < kSplitBelow;
-  if (half == 1 && !(pair_split && has_second)) return;
-  const int i0 = pair0 + half * p.qpt;                      // first query of this CTA
-  const int nqt = (half == 0 && has_second && !pair_split) ? 2 : 1;  // Q tiles of this CTA
+  const int i0 = pair0;                     // first query of this CTA
+  const int nqt = has_second ? 2 : 1;       // Q tiles of this CTA
+  // P's remainder pass for both Q tiles when the pair's first query sees few keys
   const bool split = (p.causal ? min(ceil16, qpos0 + i0 + 1) : ceil16) < kSplitBelow;
   const int i_last = min(i0 + nqt * p.qpt, q_len) - 1;
   int nvis_tile = p.causal ? min(ceil16, qpos0 + i_last + 1) : ceil16;
@@ -461,13 +459,13 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int kk = 0; kk < kBN / 16; ++kk) {
           const uint64_t bd = tc::smem_desc_sw128(base + L::oV + s * L::kTileKV + kk * 2048, L::kPanel, 1024);
-          tc::mma_ts(tmem + kColO + t * 128, tmem + kColS + t * 128 + 8 * kk, bd, idesc_pv, j > 0 || kk > 0);
+          tc::mma_ts(tmem + kColO + t * D, tmem + kColS + t * 128 + 8 * kk, bd, idesc_pv, j > 0 || kk > 0);
         }
-        if (split) {  // P's remainder, in the (idle) second Q tile's S columns
+        if (split) {  // P's remainder, from its own columns
 #pragma unroll
           for (int kk = 0; kk < kBN / 16; ++kk) {
             const uint64_t bd = tc::smem_desc_sw128(base + L::oV + s * L::kTileKV + kk * 2048, L::kPanel, 1024);
-            tc::mma_ts(tmem + kColO + t * 128, tmem + kColS + 128 + 8 * kk, bd, idesc_pv, true);
+            tc::mma_ts(tmem + kColO + t * D, tmem + kColRem + t * 64 + 8 * kk, bd, idesc_pv, true);
           }
         }
         tc::commit(bar + 8 * (kBarPFree + t));
@@ -526,7 +524,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------------ softmax
     const uint32_t taddr = tmem + ((uint32_t)(q4 * 32) << 16);
     const uint32_t col_s = kColS + qt * 128;
-    const uint32_t col_o = kColO + qt * 128;
+    const uint32_t col_o = kColO + qt * D;
     const int pos = qpos0 + qi;
     const int vis = row_valid ? (p.causal ? min(ceil16, pos + 1) : ceil16) : 0;
     const int min_vis = p.causal ? min(ceil16, qpos0 + i0 + qt * p.qpt + 1) : ceil16;
@@ -571,7 +569,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         m_ref = mb;
       }
       // P = 2^(s - m) as 16-bit pairs over the first 64 S columns (already read),
-      // its remainder (split CTAs) in the second Q tile's columns.
+      // its remainder (split pairs) in the tile's remainder columns.
       const float neg_m = m_ref == -INFINITY ? 0.f : -m_ref;
       float ls[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
@@ -596,7 +594,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const float2 f = Mma<T>::unpack(Mma<T>::pack(x[ch][2 * e], x[ch][2 * e + 1]));
             lo[e] = Mma<T>::pack(x[ch][2 * e] - f.x, x[ch][2 * e + 1] - f.y);
           }
-          tc::tmem_st16u(taddr + kColS + 128 + 16 * ch, lo);
+          tc::tmem_st16u(taddr + kColRem + qt * 64 + 16 * ch, lo);
         }
       }
       l += (ls[0] + ls[1]) + (ls[2] + ls[3]);
@@ -1283,7 +1281,7 @@ int launch_prefill(const PrefillParams& p, const void* q, int64_t q_st, int64_t 
   if (rc != SEB_OK) return rc;
   rc = kv_tensor_map(&tv, vc, dtype, p.num_blocks, p.hkv, D);
   if (rc != SEB_OK) return rc;
-  const int64_t grid = (p.unit_list ? (int64_t)p.unit_cap : (int64_t)p.num_prefill_rows * p.hkv * p.mpairs) * 2;
+  const int64_t grid = p.unit_list ? (int64_t)p.unit_cap : (int64_t)p.num_prefill_rows * p.hkv * p.mpairs;
   kern<<<(unsigned)grid, kThreads, smem, s>>>(p, tq, tk, tv);
   return launch_status("prefill_tc_kernel");
 }
@@ -1355,7 +1353,7 @@ int paged_prefill_impl(const void* q, int64_t q_stride_token, int64_t q_stride_h
   p.unit_list = unit_list;
   p.num_units = num_units;
   p.unit_cap = unit_list ? unit_cap : 0;
-  const int64_t grid = (unit_list ? (int64_t)unit_cap : (int64_t)num_prefill_rows * num_kv_heads * p.mpairs) * 2;
+  const int64_t grid = unit_list ? (int64_t)unit_cap : (int64_t)num_prefill_rows * num_kv_heads * p.mpairs;
   SEB_CHECK_ARG(grid < (1ll << 31), "seb_paged_prefill: grid too large");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   // head_dim 128: the CTA-pair kernel; head_dim 64: one CTA per pair of Q tiles

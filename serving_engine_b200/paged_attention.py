@@ -239,10 +239,11 @@ def paged_flash_attention(q, k_cache, v_cache, metadata, num_q_heads, num_kv_hea
     Rows with q_len == 1 go to the split-K decode kernel, rows with q_len > 1 to
     the tcgen05 chunked-prefill kernel (bf16/fp16, head_dim 64/128). A dict with
     this module's host-side row split (``prefill_rows``) is dispatched from the
-    host; a dict with only the reference builder's keys is split into decode
-    items and prefill units on the device (one small routing kernel, no
-    readback). Other dtypes and shapes run every token through the decode
-    kernel, which computes any row exactly.
+    host (at head_dim 64 only when it holds no prefill row); a dict with only
+    the reference builder's keys, and head_dim-64 batches with prefill rows, are
+    split into decode items and prefill units on the device (one small routing
+    kernel, no readback). Other dtypes and shapes run every token through the
+    decode kernel, which computes any row exactly.
     """
     rows = metadata["q_lens"].shape[0]
     width = int(metadata["block_table_row_stride"])
@@ -260,7 +261,12 @@ def paged_flash_attention(q, k_cache, v_cache, metadata, num_q_heads, num_kv_hea
     prefill_ok = ops.prefill_supported(q, num_q_heads, num_kv_heads) and (
         o.stride(0) % 8 == 0 and o.stride(1) % 8 == 0 and o.data_ptr() % 16 == 0)
     split = "prefill_rows" in metadata and prefill_ok
-    if not split and prefill_ok and "prefill_rows" not in metadata and q.shape[0] > rows:
+    if split and q.shape[-1] == 64 and metadata["prefill_rows"].numel():
+        # head_dim 64 runs one CTA per prefill unit: from the host split its grid
+        # spans every row's pairs up to the longest row's, most of them empty;
+        # the device router lists exactly the units the batch has.
+        split = False
+    if not split and prefill_ok and q.shape[0] > rows:
         # the reference builder's dict: route rows to the two kernels on the device
         return ops.paged_attention_routed(q, k_cache, v_cache, metadata["block_table"], metadata["q_lens"],
                                           metadata["k_lens"], metadata["q_starts"], metadata["q_pos_offsets"],
