@@ -126,7 +126,8 @@ SEB_API int seb_copy_blocks(void* kv_cache, int64_t num_layers, int64_t layer_st
  *   item_query[i]: token index of item i (NULL: item i is token i); tokens
  *                  index q/out/lse, which hold total_query tokens;
  *   item_row[i]:   its row (NULL: found by binary search over q_starts).
- *   blocks_per_split <= 0 picks a default.
+ *   blocks_per_split: at most 64 (larger requests run as 64); <= 0 picks a
+ *                  default of 8 to 40 from the batch size and table width.
  * workspace: at least seb_paged_decode_workspace_size(...) bytes, 16-byte aligned.
  *   Nothing in it needs to start at zero: its last bytes hold one arrival
  *   counter per (item, kv head), which the call clears on its stream
@@ -214,8 +215,8 @@ SEB_API int seb_paged_attention(const void* q, int64_t q_stride_token, int64_t q
  * holds until the process exits. A call whose scratch need
  * (seb_paged_decode_workspace_size) exceeds it returns SEB_EWORKSPACE with a
  * message and launches nothing. Raising blocks_per_split shrinks the need only
- * up to its cap of 32 blocks per split: the smallest need of a batch is
- *   num_items * num_q_heads * ceil(max_blocks / 32) * (head_dim + 2) * 4 bytes
+ * up to its cap of 64 blocks per split: the smallest need of a batch is
+ *   num_items * num_q_heads * ceil(max_blocks / 64) * (head_dim + 2) * 4 bytes
  *   + num_items * num_kv_heads * 4 bytes (rounded up to 16),
  * and a batch above 32 MiB even there must be split into smaller calls. The
  * call itself never calls cudaMalloc or cudaFree.

@@ -6,8 +6,8 @@
 // once per q-head of its GQA group and walks a row's whole context serially.
 //
 // Design (one warp = one work item (query item, kv head, split)):
-//   * A split is <= 32 consecutive 16-token blocks of the row; the warp keeps the
-//     split's block ids in one register per lane and streams each block's K and
+//   * A split is <= 64 consecutive 16-token blocks of the row; the warp keeps the
+//     split's block ids in two registers per lane and streams each block's K and
 //     V tiles (TMA tiled loads of 16 rows x 128-byte swizzled panels) through a
 //     STAGES-deep shared-memory ring completed on mbarriers.
 //   * All query heads of the GQA group share each KV tile: the 16 keys of a block
@@ -38,7 +38,7 @@ namespace {
 constexpr float kLn2 = 0.69314718055994530942f;
 constexpr float kLog2e = 1.44269504088896340736f;
 constexpr unsigned kFull = 0xffffffffu;
-constexpr int kMaxBps = 32;  // blocks per split: one block id per lane
+constexpr int kMaxBps = 64;  // blocks per split: two block ids per lane
 
 struct DecodeParams {
   const char* q;
@@ -146,18 +146,29 @@ __device__ __forceinline__ void report_item(const DecodeParams& p, const ItemInf
   else if ((int64_t)((it.k_len + 15) >> 4) > p.max_blocks) atomic_or_err(p.err, SEB_ERRBIT_KLEN);
 }
 
-// Block ids of blocks [b0, b0 + nb) of the row, one per lane; -1 when out of range.
-__device__ __forceinline__ int load_block_ids(const DecodeParams& p, const ItemInfo& it, int b0,
-                                              int nb, int lane) {
-  int bid = -1;
-  if (lane < nb) {
-    bid = __ldg(p.block_table + (int64_t)it.row * p.bt_stride + b0 + lane);
-    if (bid < 0 || (int64_t)bid >= p.num_blocks) {
-      atomic_or_err(p.err, SEB_ERRBIT_BLOCK_ID);
-      bid = -1;
-    }
+// Block ids of blocks [b0, b0 + nb) of the row (nb <= 64): lane l holds blocks
+// b0 + l and b0 + 32 + l; -1 when out of range.
+struct BlockIds {
+  int lo, hi;
+  // Id of block b0 + j (j warp-uniform).
+  __device__ __forceinline__ int get(int j) const { return __shfl_sync(0xffffffffu, j < 32 ? lo : hi, j & 31); }
+};
+
+__device__ __forceinline__ int load_block_id(const DecodeParams& p, const ItemInfo& it, int blk) {
+  int bid = __ldg(p.block_table + (int64_t)it.row * p.bt_stride + blk);
+  if (bid < 0 || (int64_t)bid >= p.num_blocks) {
+    atomic_or_err(p.err, SEB_ERRBIT_BLOCK_ID);
+    bid = -1;
   }
   return bid;
+}
+
+__device__ __forceinline__ BlockIds load_block_ids(const DecodeParams& p, const ItemInfo& it, int b0, int nb,
+                                                   int lane) {
+  BlockIds ids{-1, -1};
+  if (lane < nb) ids.lo = load_block_id(p, it, b0 + lane);
+  if (lane + 32 < nb) ids.hi = load_block_id(p, it, b0 + 32 + lane);
+  return ids;
 }
 
 // --------------------------------------------------------------------------
@@ -321,7 +332,7 @@ __global__ void __launch_bounds__(WARPS * 32)
   if (split >= max(it.n_splits, 1)) return;
   const int b0 = split * p.bps;
   const int nb = min(p.bps, it.nblk - b0);  // <= 0 only when the row has no keys
-  const int bid_reg = load_block_ids(p, it, b0, max(nb, 0), lane);
+  const BlockIds bids = load_block_ids(p, it, b0, max(nb, 0), lane);
 
   // Q^T as the B operand (k = head dims, n = heads of the group), kept in registers.
   uint32_t qf[KS][NTH][2];
@@ -357,7 +368,7 @@ __global__ void __launch_bounds__(WARPS * 32)
 
   // Stage block j (relative to b0) into ring slot j % STAGES (lane 0 issues).
   auto issue = [&](int j) {
-    const int bid = __shfl_sync(kFull, bid_reg, j);
+    const int bid = bids.get(j);
     if (lane == 0) {
       const int s = j % STAGES;
       const uint32_t bar = bar0 + 8 * s;
@@ -415,7 +426,7 @@ __global__ void __launch_bounds__(WARPS * 32)
     const uint32_t sk = ring + s * Tile::kStage;
     const uint32_t sv = sk + Tile::kTile;
     const int blk = b0 + j;
-    const bool bad = __shfl_sync(kFull, bid_reg, j) < 0;
+    const bool bad = bids.get(j) < 0;
     const int real = bad ? 0 : min(16, it.k_len - blk * 16);
     if (real < 16) {
       // V rows of zero-padded or unreadable keys must be exact zeros: the pool
@@ -617,7 +628,7 @@ __global__ void __launch_bounds__(WARPS * 32) decode_simt_kernel(const DecodePar
   if (split >= max(it.n_splits, 1)) return;
   const int b0 = split * p.bps;
   const int nb = min(p.bps, it.nblk - b0);
-  const int bid_reg = load_block_ids(p, it, b0, max(nb, 0), lane);
+  const BlockIds bids = load_block_ids(p, it, b0, max(nb, 0), lane);
 
   float qv[GMAX][DL];
   const T* qbase = reinterpret_cast<const T*>(p.q) + (int64_t)it.qtok * p.q_st;
@@ -642,7 +653,7 @@ __global__ void __launch_bounds__(WARPS * 32) decode_simt_kernel(const DecodePar
   const T* vc = reinterpret_cast<const T*>(p.v_cache);
   for (int j = 0; j < nb; ++j) {
     const int blk = b0 + j;
-    const int bid = __shfl_sync(kFull, bid_reg, j);
+    const int bid = bids.get(j);
     const int vis = min(16, it.n_vis - blk * 16);
     const int real = bid >= 0 ? min(vis, it.k_len - blk * 16) : 0;
     for (int r = 0; r < vis; ++r) {
@@ -732,16 +743,24 @@ constexpr int kSimtWarps = 4;
 // Bytes of the split counters at the end of the decode workspace.
 int64_t counter_bytes(int64_t num_items, int64_t hkv) { return ((num_items * hkv * 4 + 15) / 16) * 16; }
 
+// Longest split the automatic rule picks. Measured over 200 calls: config 2
+// (64 rows, k_len U[1024, 8192], head_dim 128) 221.5 / 217.9 / 217.0 us at 32 /
+// 40 / 64 blocks; config-4 decode rows (256 rows, lognormal lengths, head_dim
+// 64, a 264-block table) 78.7 / 74.5 / 84.1 us: longer splits cut the merges
+// and the idle CTAs of a wide table, but past about 40 blocks a short batch's
+// last splits run alone.
+constexpr int kAutoMaxBps = 40;
+
 int choose_bps(int num_items, int hkv, int64_t max_blocks, int requested) {
   if (requested > 0) return requested > kMaxBps ? kMaxBps : requested;
   // Aim for about two waves of 12 resident warps per SM, assuming rows fill
-  // about half of the block-table width; long splits (up to 32 blocks) keep
-  // the partial-result traffic small, >= 8 blocks keep the copy ring busy.
+  // about half of the block-table width; long splits (up to kAutoMaxBps blocks)
+  // keep the partial-result traffic small, >= 8 blocks keep the copy ring busy.
   const double est_blocks = 0.5 * (double)num_items * hkv * (double)max_blocks;
   const double slots = (double)num_sms() * 12.0 * 2.0;
   int bps = (int)std::ceil(est_blocks / slots);
   if (bps < 8) bps = 8;
-  if (bps > kMaxBps) bps = kMaxBps;
+  if (bps > kAutoMaxBps) bps = kAutoMaxBps;
   return bps;
 }
 

@@ -530,7 +530,11 @@ class E2EEngine:
     @torch.inference_mode()
     def capture_graphs(self, buckets=None) -> None:
         """Capture one decode-step graph per batch-size bucket (largest first, so
-        the decode workspace is allocated at its largest size before capture)."""
+        the decode workspace is allocated at its largest size before capture),
+        and replay each once: the first launch of an instantiated graph uploads
+        it to the device (tens of milliseconds for the 256-row step), which
+        belongs to start-up, not to the first decode step. The replay runs pad
+        rows only, whose KV writes land on the scratch block."""
         if not self.use_graphs:
             raise RuntimeError("engine built without use_graphs")
         limit = self.sched.max_seqs or max(self.GRAPH_BUCKETS)
@@ -549,6 +553,7 @@ class E2EEngine:
             g = torch.cuda.CUDAGraph()
             with torch.cuda.graph(g, pool=pool):
                 st["out"] = self._run_graph_body(st)
+            g.replay()
             st["graph"] = g
             self.graphs[bucket] = st
         torch.cuda.synchronize(self.device)

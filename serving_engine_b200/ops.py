@@ -98,14 +98,18 @@ def check_device_errors(dev: torch.device | None = None, reset: bool = True) -> 
 
 
 def workspace(dev: torch.device, nbytes: int) -> torch.Tensor:
-    """A per-device scratch buffer of at least nbytes, grown on demand."""
+    """A per-device scratch buffer of at least nbytes, grown on demand to at
+    least twice its size, so a run whose batches grow step by step reallocates
+    a few times rather than at every step."""
     idx = dev.index if dev.index is not None else torch.cuda.current_device()
     ws = _workspaces.get(idx)
     if ws is None or ws.numel() < nbytes:
+        size = max(nbytes, 1 << 20)
         if ws is not None:
             _retired_workspaces.append(ws)
+            size = max(size, 2 * ws.numel())
         with torch.inference_mode(False):
-            ws = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=torch.device("cuda", idx))
+            ws = torch.empty(size, dtype=torch.uint8, device=torch.device("cuda", idx))
         _workspaces[idx] = ws
     return ws
 

@@ -114,4 +114,4 @@ def test_noalloc_rejects_a_call_beyond_its_scratch():
                                       None, 0, 0, None, 0, None, None)
     assert st == _lib.SEB_EWORKSPACE
     msg = lib.seb_last_error()
-    assert b"built-in scratch" in msg and b"capped at 32" in msg
+    assert b"built-in scratch" in msg and b"capped at 64" in msg
