@@ -123,7 +123,7 @@ enum {
   kBarVEmpty = 7,  // +stage: PV of every Q tile consumed V
   kBarSFull = 9,   // +Q tile: S(t, j) complete (and every earlier MMA)
   kBarPFull = 11,  // +Q tile: the tile's 4 softmax warps stored P(t, j)
-  kBarPFree = 13,  // +Q tile: PV(t, j) complete: S/P columns reusable, O final
+  kBarPFree = 13,  // +Q tile: unused (S follows P V in the one issuing thread's order)
   kBarDone = 15,
   kNumBars = 16
 };
@@ -350,7 +350,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int t = 0; t < kQT; ++t) {
       mbar_init(bar + 8 * (kBarSFull + t), 1);
       mbar_init(bar + 8 * (kBarPFull + t), 4);
-      mbar_init(bar + 8 * (kBarPFree + t), 1);
     }
     mbar_init(bar + 8 * kBarDone, 1);
     fence_mbar_init();
@@ -468,13 +467,14 @@ __global__ void __launch_bounds__(kThreads, 1)
             tc::mma_ts(tmem + kColO + t * D, tmem + kColRem + t * 64 + 8 * kk, bd, idesc_pv, true);
           }
         }
-        tc::commit(bar + 8 * (kBarPFree + t));
       }
       __syncwarp();
     };
     // Ping-pong: per KV tile j and Q tile t, PV(t, j) then S(t, j+1), so one Q
     // tile's softmax runs while the other tile's MMAs execute. S(t, j+1)
-    // overwrites the columns PV(t, j) reads P from: it waits for PV(t, j).
+    // overwrites the columns PV(t, j) reads P from; both are issued by this one
+    // thread, and the tensor pipe runs one thread's MMAs in issue order, so
+    // S(t, j+1) follows PV(t, j) at once (no wait for PV(t, j) to complete).
     if (wait_or_flag(bar + 8 * kBarKFull, 0, failed)) {
       for (int t = 0; t < nqt; ++t) issue_s(t, 0);
       if (lane == 0) tc::commit(bar + 8 * kBarKEmpty);
@@ -506,7 +506,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         issue_pv(t, j);
         if (!next) continue;
         if (t == 0 && !wait_or_flag(bar + 8 * (kBarKFull + sk), ((j + 1) / kKStages) & 1, failed)) break;
-        if (!wait_or_flag(bar + 8 * (kBarPFree + t), j & 1, failed)) break;
         tc::fence_after_sync();
         issue_s(t, j + 1);
       }
