@@ -120,14 +120,25 @@ def test_shapes_vs_oracle(dtype, hq, hkv, d):
     assert_close(o, lse, o_ref, lse_ref, dtype)
 
 
-@pytest.mark.parametrize("bps", [1, 3, 8, 32])
+@pytest.mark.parametrize("bps", [1, 3, 8, 32, 33, 40, 64, 100])
 def test_split_sizes_agree(bps):
-    """Every split size (1 block .. 32 blocks per split, hence 1 .. many splits and the
-    in-kernel merge of the splits) gives the oracle's answer."""
+    """Every split size (1 block .. 64 blocks per split, the cap a larger request is
+    held to; hence 1 .. many splits and the in-kernel merge of the splits; past 32
+    blocks each lane holds a second block id) gives the oracle's answer."""
     b = workloads.decode_batch(6, 1, 1200, 32, 8, 128, torch.bfloat16, seed=40 + bps, num_blocks=600)
     o, lse = run_b200(b, blocks_per_split=bps)
     o_ref, lse_ref = run_oracle(b)
     assert_close(o, lse, o_ref, lse_ref, torch.bfloat16)
+
+
+@pytest.mark.parametrize("dtype,d", [(torch.float32, 128), (torch.bfloat16, 64), (torch.float16, 256)])
+def test_long_splits_other_paths(dtype, d):
+    """Splits of 48 blocks (second block id per lane) on the CUDA-core path (fp32)
+    and the tensor-core path at head_dims 64 and 256."""
+    b = workloads.decode_batch(5, 700, 1500, 16, 4, d, dtype, seed=77 + d, num_blocks=600)
+    o, lse = run_b200(b, blocks_per_split=48)
+    o_ref, lse_ref = run_oracle(b)
+    assert_close(o, lse, o_ref, lse_ref, dtype)
 
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
