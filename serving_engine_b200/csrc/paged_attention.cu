@@ -69,10 +69,15 @@ __device__ __forceinline__ int block_exclusive_scan(int v, int* warp_sums, int* 
 
 // Rows in order; decode items keep the rows' order, and each prefill row's units
 // are its kv heads, each with its Q-tile pairs latest first (they see the most
-// keys), the order the prefill kernel's own row x kv head x pair grid uses.
+// keys), the order the prefill kernel's own row x kv head x pair grid uses. The
+// scans give each row its place; one warp per row then writes the row's units
+// (a 4,096-token row at head_dim 64 has 512 of them), 32 lanes at a time.
 __global__ void __launch_bounds__(kRouteThreads) route_rows_kernel(const RouteParams r) {
   __shared__ int warp_sums[32];
   __shared__ int totals[2];
+  __shared__ int s_off[kRouteThreads], s_n[kRouteThreads], s_mp[kRouteThreads];
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
   int dec_base = 0, unit_base = 0;
   for (int r0 = 0; r0 < r.num_rows; r0 += kRouteThreads) {
     const int row = r0 + threadIdx.x;
@@ -95,20 +100,28 @@ __global__ void __launch_bounds__(kRouteThreads) route_rows_kernel(const RoutePa
       r.dec_tokens[dec_off] = q_start;
       r.dec_rows[dec_off] = row;
     }
-    for (int k = 0; k < nunits; ++k) {
-      const int u = unit_off + k;
-      if (u >= r.unit_cap) {  // cannot happen with the host's bound; never write past the list
-        atomic_or_err(r.err, SEB_ERRBIT_META);
-        break;
+    s_off[threadIdx.x] = unit_off;
+    s_n[threadIdx.x] = nunits;
+    s_mp[threadIdx.x] = mp;
+    __syncthreads();
+    const int chunk_rows = min(kRouteThreads, r.num_rows - r0);
+    for (int i = warp; i < chunk_rows; i += kRouteThreads / 32) {
+      const int n = s_n[i], off = s_off[i], m = s_mp[i];
+      for (int k = lane; k < n; k += 32) {
+        const int u = off + k;
+        if (u >= r.unit_cap) {  // cannot happen with the host's bound; never write past the list
+          atomic_or_err(r.err, SEB_ERRBIT_META);
+          break;
+        }
+        const int kvh = k / m;
+        const int pr = m - 1 - (k % m);
+        r.units[2 * u] = r0 + i;
+        r.units[2 * u + 1] = (pr << 8) | kvh;
       }
-      const int kvh = k / mp;
-      const int pr = mp - 1 - (k % mp);
-      r.units[2 * u] = row;
-      r.units[2 * u + 1] = (pr << 8) | kvh;
     }
     dec_base += totals[0];
     unit_base += totals[1];
-    __syncthreads();  // totals is rewritten by the next chunk's scans
+    __syncthreads();  // totals and the row arrays are rewritten by the next chunk
   }
   if (threadIdx.x == 0) {
     r.counts[0] = dec_base;
