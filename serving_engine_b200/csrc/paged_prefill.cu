@@ -206,9 +206,11 @@ __device__ __forceinline__ float2 poly_exp2x2(float2 x) {
 
 // Pairs of a 32-score chunk (bit e: scores 2e, 2e + 1) whose exponentials the
 // pair kernel evaluates with poly_exp2 on unmasked tiles of pairs without the
-// remainder pass.
+// remainder pass: 5 of 16. Config 3 on one box, 100 steps, two runs each:
+// 3 of 16 (0x4210) 932.6 / 933.4 TFLOP/s, 4 (0x8888) 972.2 / 971.4, 5 (0x8A22)
+// 979.2 / 978.8, 6 (0x9249) 912.9 / 912.7.
 #ifndef SEB_POLY_PAIRS
-#define SEB_POLY_PAIRS 0x8888u
+#define SEB_POLY_PAIRS 0x8A22u
 #endif
 constexpr unsigned kPolyPairs = SEB_POLY_PAIRS;
 
