@@ -318,7 +318,12 @@ class E2EEngine:
         self.trace: list[dict] = []
         self.record_logits = record_logits
         self.record_trace = record_trace
-        self._pending: dict | None = None  # the newest graph step whose tokens are not on the host yet
+        self._pending: dict | None = None  # the newest launched step whose tokens are not on the host yet
+        self._eager_hosts: list | None = None  # pinned token buffers of pipelined eager steps, used in turn
+        self._eager_turn = 0
+        self._stage: list = [None, None]  # pinned input staging of eager steps (int64, int32), used in turn
+        self._stage_ev: list = [None, None]
+        self._stage_turn = 0
         # steps through the fused layer kernels instead of the HF modules
         self.fused = None
         if fused_steps:
@@ -363,10 +368,16 @@ class E2EEngine:
             if any(s.eos is not None for s, _ in plan.rows):
                 self._drain()  # the end-of-sequence check below needs the values
             emitted = len(plan.rows)
+        elif self._can_pipeline(plan):
+            # eager step launched without waiting, like the graph steps: a row whose
+            # newest token the previous step produced takes it on the device, and
+            # this step's tokens reach the host while the next step's inputs are
+            # prepared and launched
+            emitted = self._eager_launch(plan, previous)
         else:
             self._drain()  # a prefill row may need the real values of earlier tokens
             previous = None
-            next_tok = self._eager_step(plan.rows)
+            next_tok = self._eager_step(plan.rows).tolist()
             emitted = 0
             for (s, c), tok in zip(plan.rows, next_tok):
                 if c is None or s.rid in plan.final:
@@ -384,26 +395,88 @@ class E2EEngine:
         return emitted
 
     def _drain(self, pending: dict | None = None) -> None:
-        """Wait for a launched graph step's tokens (default: the newest) and write
-        them over its placeholders."""
+        """Wait for a launched step's tokens (default: the newest) and write them
+        over its placeholders (rows whose index is None sampled nothing)."""
         pending = self._pending if pending is None else pending
         if pending is None:
             return
         pending["event"].synchronize()
         values = pending["host"][:len(pending["rows"])].tolist()
         for (s, idx), v in zip(pending["rows"], values):
-            s.out[idx] = v
+            if idx is not None:
+                s.out[idx] = v
         if pending is self._pending:
             self._pending = None
 
-    def _eager_step(self, rows) -> list:
+    def _can_pipeline(self, plan: StepPlan) -> bool:
+        """An eager step may run ahead of the host when no value of a sampled token
+        is needed before it runs: no logits are recorded, no row stops at an
+        end-of-sequence token, and no prefill chunk re-reads an output token whose
+        value is still on the device (a recomputed, preempted request)."""
+        if self.record_logits:
+            return False
+        for s, c in plan.rows:
+            if s.eos is not None or (c is not None and c > 0 and None in s.out):
+                return False
+        return True
+
+    def _eager_launch(self, plan: StepPlan, previous: dict | None) -> int:
+        """Launch an eager step and leave its tokens pending (placeholders in each
+        sampling row's output); returns the number of tokens sampled."""
+        rows = plan.rows
+        nxt = self._eager_step(rows, previous)
+        n = len(rows)
+        if self._eager_hosts is None or self._eager_hosts[0].numel() < n:
+            self._eager_hosts = [torch.zeros(max(n, 256), dtype=torch.int64).pin_memory() for _ in range(2)]
+        host = self._eager_hosts[self._eager_turn]
+        self._eager_turn ^= 1
+        host[:n].copy_(nxt, non_blocking=True)
+        ev = torch.cuda.Event()
+        ev.record()
+        placed, emitted = [], 0
+        for s, c in rows:
+            if c is None or s.rid in plan.final:
+                placed.append((s, len(s.out)))
+                s.out.append(None)
+                emitted += 1
+            else:
+                placed.append((s, None))
+        self._pending = {"rows": placed, "host": host, "event": ev, "st": {"out": nxt},
+                         "row_of": {s.rid: i for i, (s, _) in enumerate(rows)}}
+        return emitted
+
+    def _staging(self, n64: int, n32: int) -> tuple:
+        """The next pinned staging set (int64 and int32 buffers of at least n64 and
+        n32 elements), once the copies that last read it have run."""
+        k = self._stage_turn
+        self._stage_turn ^= 1
+        if self._stage_ev[k] is not None:
+            self._stage_ev[k].synchronize()
+        st = self._stage[k]
+        if st is None or st[0].numel() < n64 or st[1].numel() < n32:
+            c64 = max(n64, 2 * st[0].numel() if st is not None else 0, 1 << 16)
+            c32 = max(n32, 2 * st[1].numel() if st is not None else 0, 1 << 16)
+            st = (torch.empty(c64, dtype=torch.int64).pin_memory(), torch.empty(c32, dtype=torch.int32).pin_memory())
+            self._stage[k] = st
+        return st
+
+    def _eager_step(self, rows, previous: dict | None = None) -> torch.Tensor:
+        """One step through the model with host-built inputs; returns the greedy
+        token of each row's last position, on the device. A decode row whose
+        newest token is a placeholder of `previous` (a launched step) takes its
+        value from that step's device output."""
         toks, pos, slots = [], [], []
         q_lens, k_lens, q_pos = [], [], []
+        gather = []  # (token index, row of the previous step's output)
         for s, chunk in rows:
             seq_toks = s.tokens()
             if chunk is None or chunk == 0:  # the newest token (a decode row, or a fully cached prompt)
                 p0, n = s.total_len - 1, 1
-                toks.append(seq_toks[-1])
+                t = seq_toks[-1]
+                if t is None:
+                    gather.append((len(toks), previous["row_of"][s.rid]))
+                    t = 0
+                toks.append(t)
             else:
                 p0, n = s.computed, chunk
                 toks.extend(seq_toks[p0:p0 + n])
@@ -416,11 +489,34 @@ class E2EEngine:
             q_pos.append(p0)
         starts = np.concatenate(([0], np.cumsum(q_lens)[:-1])).tolist()
         dev = self.device
-        ids = torch.from_numpy(np.asarray(toks, dtype=np.int64)).pin_memory().to(dev, non_blocking=True)
-        pos_t = torch.from_numpy(np.concatenate(pos)).pin_memory().to(dev, non_blocking=True)
-        slot_t = torch.from_numpy(np.concatenate(slots)).pin_memory().to(dev, non_blocking=True)
-        md = PackedMetadata(q_lens, k_lens, starts, q_pos, [s.table for s, _ in rows]).upload(dev)
-        last = torch.from_numpy(np.cumsum(q_lens) - 1).pin_memory().to(dev, non_blocking=True)
+        packed = PackedMetadata(q_lens, k_lens, starts, q_pos, [s.table for s, _ in rows])
+        # token ids, positions, slots, last-token indices and (when needed) the
+        # gather rows in one int64 staging buffer, the metadata in an int32 one:
+        # two pinned sets used in turn, each rewritten only once its previous
+        # copies have run (a launched step may still be reading the other set)
+        nt, nr = len(toks), len(rows)
+        n64 = 4 * nt + nr
+        st64, st32 = self._staging(n64, packed.host.numel())
+        a = st64.numpy()
+        a[0:nt] = toks
+        a[nt:2 * nt] = np.concatenate(pos)
+        a[2 * nt:3 * nt] = np.concatenate(slots)
+        a[3 * nt:3 * nt + nr] = np.cumsum(q_lens) - 1
+        if gather:
+            src = a[3 * nt + nr:n64]
+            src[:] = -1
+            for ti, pi in gather:
+                src[ti] = pi
+        d64 = st64[:n64].to(dev, non_blocking=True)
+        md = packed.upload(dev, staging=st32)
+        self._stage_ev[self._stage_turn ^ 1] = torch.cuda.Event()
+        self._stage_ev[self._stage_turn ^ 1].record()
+        ids, pos_t, slot_t = d64[0:nt], d64[nt:2 * nt], d64[2 * nt:3 * nt]
+        last = d64[3 * nt:3 * nt + nr]
+        if gather:
+            src_t = d64[3 * nt + nr:n64]
+            picked = previous["st"]["out"].index_select(0, src_t.clamp(min=0))
+            ids = torch.where(src_t >= 0, picked, ids)
         if self.fused is not None:
             logits = self.fused.logits(ids, pos_t, slot_t, self.kv_cache, md, last)
         else:
@@ -434,7 +530,7 @@ class E2EEngine:
             for i, (s, c) in enumerate(rows):
                 if c is None or (s.computed + c >= s.total_len):
                     self.logit_log.append((s.rid, len(s.out), ids5[i], vals5[i]))
-        return logits.argmax(dim=-1).tolist()
+        return logits.argmax(dim=-1)
 
     # ------------------------------------------------------------ CUDA graphs
     def _graph_inputs(self, bucket: int) -> dict:

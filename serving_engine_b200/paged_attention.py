@@ -130,9 +130,17 @@ class PackedMetadata:
     def nbytes(self) -> int:
         return self.host.numel() * 4
 
-    def upload(self, device="cuda") -> dict:
+    def upload(self, device="cuda", staging: torch.Tensor | None = None) -> dict:
+        """Copy the buffer to `device` (one host-to-device copy) and return the
+        metadata dict over it. `staging`: a pinned int32 host buffer of at least
+        the packed size to copy through (the caller keeps it unwritten until the
+        copy has run); otherwise the buffer is pinned for the copy."""
         dev = torch.device(device)
-        if dev.type == "cuda":
+        if dev.type == "cuda" and staging is not None:
+            st = staging[:self.host.numel()]
+            st.copy_(self.host)
+            buf = st.to(dev, non_blocking=True)
+        elif dev.type == "cuda":
             buf = (self.host if self.host.is_pinned() else self.host.pin_memory()).to(dev, non_blocking=True)
         else:
             buf = self.host.clone()
