@@ -74,6 +74,8 @@ def parse_args():
     ap.add_argument("--prefix-len", type=int, default=2040,
                     help="prefill: tokens of the shared prefix (config 3: 2040; 0: fresh prompts)")
     ap.add_argument("--chunk-len", type=int, default=512, help="prefill: tokens each row prefills (config 3: 512)")
+    ap.add_argument("--head-dim", type=int, default=128, choices=[64, 128],
+                    help="prefill: head_dim (config 3: 128, the CTA-pair kernel; 64: the config-4 head shape)")
     return ap.parse_args()
 
 
@@ -606,7 +608,8 @@ def run_prefill_workload(args, device, steps: int | None = None):
     from serving_engine_b200 import ops, paged_flash_attention, workloads
     from serving_engine_b200.paged_attention import metadata_from_lists
 
-    b = workloads.prefix_prefill_batch(16, args.prefix_len, args.chunk_len, 32, 8, 128, torch.bfloat16, args.seed,
+    d = args.head_dim
+    b = workloads.prefix_prefill_batch(16, args.prefix_len, args.chunk_len, 32, 8, d, torch.bfloat16, args.seed,
                                        fill=str(device))
     md = metadata_from_lists(b.q_lens, b.k_lens, b.q_starts, b.q_pos_offsets, b.block_tables, device)
     q = b.q.to(device)
@@ -647,15 +650,15 @@ def run_prefill_workload(args, device, steps: int | None = None):
     peaks_path = REPO / "MEASURED_PEAKS.json"
     pk = json.loads(peaks_path.read_text()) if peaks_path.exists() else {"bf16_tflops": 1590.0}
     app_bytes = 2 * 2 * nk.numel() * nk.element_size()
-    cow_bytes = 2 * 2 * len(b.extra["cow_dst"]) * 16 * 8 * 128 * 2
+    cow_bytes = 2 * 2 * len(b.extra["cow_dst"]) * 16 * 8 * d * 2
     return {
         "metric": "chunked-prefill attention TFLOP/s (config 3)", "value": round(tflops, 1), "unit": "TFLOP/s",
         "n_gpus": 1, "steps": n, "warmup": args.warmup, "ms_per_step": round(att_ms + cow_ms + app_ms, 4),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
         "config": {"workload": (f"config 3: 16 rows, shared {args.prefix_len}-token prefix, {args.chunk_len}-token causal "
-                                "chunks, 32q/8kv, D=128") if (args.prefix_len, args.chunk_len) == (2040, 512) else
+                                f"chunks, 32q/8kv, D={d}") if (args.prefix_len, args.chunk_len, d) == (2040, 512, 128) else
                    (f"config-3 variant: 16 rows, shared {args.prefix_len}-token prefix, {args.chunk_len}-token causal "
-                    "chunks, 32q/8kv, D=128"),
+                    f"chunks, 32q/8kv, D={d}"),
                    "attention_gflop": round(flops / 1e9, 1)},
         "breakdown_ms": {"cow_copy_blocks": round(cow_ms, 4), "kv_append": round(app_ms, 4),
                          "prefill_attention": round(att_ms, 4)},
@@ -664,7 +667,8 @@ def run_prefill_workload(args, device, steps: int | None = None):
         "roofline": {"bound": "tensor", "achieved": round(tflops, 1), "peak": pk.get("bf16_tflops"),
                      "unit": "TFLOP/s", "frac": round(tflops / pk.get("bf16_tflops", 1590.0), 4),
                      "peak_source": "measured burst (MEASURED_PEAKS.json bf16_tflops)",
-                     "traffic": profiled_traffic("prefill_pair_kernel"), "traffic_unit": "dram bytes per launch"},
+                     "traffic": profiled_traffic("prefill_pair_kernel") if d == 128 else None,
+                     "traffic_unit": "dram bytes per launch"},
     }
 
 
