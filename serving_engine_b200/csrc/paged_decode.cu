@@ -1015,8 +1015,8 @@ extern "C" int seb_paged_decode_noalloc(const void* q, int64_t q_stride_token, i
   const int64_t need = seb_paged_decode_workspace_size(num_items, num_q_heads, num_kv_heads, head_dim, max_blocks,
                                                        blocks_per_split);
   if (need > (int64_t)SEB_NOALLOC_SCRATCH_BYTES) {
-    // The smallest need any blocks_per_split reaches is the one at the cap of 32
-    // blocks per split; past it only a smaller batch helps.
+    // The smallest need any blocks_per_split reaches is the one at the cap of
+    // kMaxBps blocks per split; past it only a smaller batch helps.
     const int64_t floor_need = seb_paged_decode_workspace_size(num_items, num_q_heads, num_kv_heads, head_dim,
                                                                max_blocks, kMaxBps);
     set_error("seb_paged_decode_noalloc: this call needs %lld bytes of split-K scratch but the built-in scratch "
