@@ -16,9 +16,11 @@
 // prefill_pair_kernel (head_dim 128) runs a unit on a cluster of two CTAs whose
 // MMAs span both SMs (tcgen05 cta_group::2); it is described above the kernel.
 //
-// prefill_tc_kernel (head_dim 64) runs a unit in one CTA:
-//   warp 0     TMA producer: the Q tiles once, then K and V tiles (block ids
-//              prefetched a window ahead) into 2-stage rings;
+// prefill_tc_kernel (head_dim 64) runs a unit in one CTA, persistent (one CTA
+// per SM walks units c, c + grid, ...; Q double-buffered, the rings and barrier
+// phases running on from unit to unit):
+//   warp 0     TMA producer: the unit's Q tiles, then K and V tiles (block ids
+//              prefetched a window ahead) into 3-stage rings;
 //   warp 1     owns TMEM (512 columns: per Q tile, S of 128 columns with P
 //              written over its first 64 as 16-bit pairs, O of 64 columns and
 //              64 columns for P's remainder) and issues the MMAs from one
@@ -54,8 +56,8 @@ constexpr int kBM = 128;       // MMA rows per Q tile
 constexpr int kBN = 128;       // keys per KV tile (8 paged blocks)
 constexpr int kQT = 2;         // Q tiles per CTA: each K/V tile feeds 256 rows
 constexpr int kThreads = 320;  // producer, MMA, one softmax warpgroup per Q tile
-constexpr int kKStages = 2;    // K ring depth
-constexpr int kVStages = 2;    // V ring depth
+constexpr int kKStages = 3;    // K ring depth (the rings run on from unit to unit)
+constexpr int kVStages = 3;    // V ring depth
 constexpr int kTmemCols = 512;
 // TMEM columns of Q tile t (head_dim 64): S at t * 128 (128 fp32 scores per row;
 // P overwrites its first 64 columns as packed 16-bit pairs), O at 256 + t * 64,
@@ -107,26 +109,28 @@ struct PrefillLayout {
   static constexpr int kPanel = 128 * 128;    // 128 rows x 128 bytes
   static constexpr int kTileQ = kPanels * kPanel;
   static constexpr int kTileKV = kPanels * kPanel;
-  static constexpr int oQ = 0;                // [Q tile]
-  static constexpr int oK = oQ + kQT * kTileQ;  // [stage]
+  static constexpr int oQ = 0;                      // [Q buffer (2)][Q tile]
+  static constexpr int oK = oQ + 2 * kQT * kTileQ;  // [stage]
   static constexpr int oV = oK + kKStages * kTileKV;
   static constexpr int oBar = oV + kVStages * kTileKV;
   static constexpr int kBytes = oBar + 256;
 };
 
-// mbarrier slots
+// mbarrier slots of prefill_tc_kernel
 enum {
-  kBarQ = 0,
-  kBarKFull = 1,   // +stage (2)
-  kBarKEmpty = 3,  // +stage: S of every Q tile consumed K
-  kBarVFull = 5,   // +stage (2)
-  kBarVEmpty = 7,  // +stage: PV of every Q tile consumed V
-  kBarSFull = 9,   // +Q tile: S(t, j) complete (and every earlier MMA)
-  kBarPFull = 11,  // +Q tile: the tile's 4 softmax warps stored P(t, j)
-  kBarPFree = 13,  // +Q tile: unused (S follows P V in the one issuing thread's order)
-  kBarDone = 15,
-  kNumBars = 16
+  kBarQFull = 0,                       // +Q buffer (2): the unit's Q tiles landed
+  kBarQEmpty = 2,                      // +Q buffer: the unit's last S done, Q may be reloaded
+  kBarKFull = 4,                       // +stage
+  kBarKEmpty = kBarKFull + kKStages,   // +stage: S of every Q tile consumed K
+  kBarVFull = kBarKEmpty + kKStages,   // +stage
+  kBarVEmpty = kBarVFull + kVStages,   // +stage: PV of every Q tile consumed V
+  kBarSFull = kBarVEmpty + kVStages,   // +Q tile: S(t, j) complete (and every earlier MMA)
+  kBarPFull = kBarSFull + kQT,         // +Q tile: the tile's 4 softmax warps stored P(t, j)
+  kBarODone = kBarPFull + kQT,         // +Q tile: the unit's last PV(t) complete, O(t) final
+  kBarFinal = kBarODone + kQT,         // every MMA complete before TMEM is released
+  kNumBars = kBarFinal + 1
 };
+static_assert(kNumBars * 8 + 8 <= 256, "barrier region");
 
 // Barrier `id` (1..15) over `n` threads (a multiple of 32) of the CTA.
 __device__ __forceinline__ void named_bar_sync(int id, int n) {
@@ -257,6 +261,63 @@ __device__ __forceinline__ void mask_chunk_causal(float (&x)[32], int key0, int 
   for (int i = 0; i < 32; ++i) x[i] = i < lim ? x[i] : -INFINITY;
 }
 
+// One work unit (prefill row, kv head, pair of Q tiles), decoded identically by
+// every role of either kernel.
+struct PairUnit {
+  int row, kvh, q_len, q_start, k_len, qpos0, ceil16, pair0, i_last, nblk, ntiles;
+  bool split;
+};
+
+// Decodes unit u; false: the unit does nothing (no such row or pair). Without a
+// unit list, a row's pairs are visited late-first (they are the longest).
+__device__ __forceinline__ bool pair_unit(const PrefillParams& p, int u, PairUnit& w) {
+  int pr;
+  if (p.unit_list) {
+    w.row = __ldg(p.unit_list + 2 * u);
+    const int e = __ldg(p.unit_list + 2 * u + 1);
+    w.kvh = e & 255;
+    pr = e >> 8;
+  } else {
+    pr = p.mpairs - 1 - (u % p.mpairs);
+    u /= p.mpairs;
+    w.kvh = u % p.hkv;
+    const int prow = u / p.hkv;
+    if (prow >= p.num_prefill_rows) return false;
+    w.row = p.rows ? __ldg(p.rows + prow) : prow;
+  }
+  if (w.row < 0 || w.row >= p.num_rows) return false;
+  w.q_len = __ldg(p.q_lens + w.row);
+  w.q_start = __ldg(p.q_starts + w.row);
+  w.k_len = max(__ldg(p.k_lens + w.row), 0);
+  w.qpos0 = __ldg(p.q_pos + w.row);
+  w.ceil16 = (w.k_len + 15) & ~15;
+  w.pair0 = pr * kQT * p.qpt;
+  if (w.pair0 >= w.q_len) return false;
+  w.i_last = min(w.pair0 + kQT * p.qpt, w.q_len) - 1;
+  w.split = (p.causal ? min(w.ceil16, w.qpos0 + w.pair0 + 1) : w.ceil16) < kSplitBelow;
+  const int nvis = max(p.causal ? min(w.ceil16, w.qpos0 + w.i_last + 1) : w.ceil16, 0);
+  w.nblk = min((nvis + 15) >> 4, (int)p.max_blocks);
+  w.ntiles = (w.nblk + 7) >> 3;
+  return true;
+}
+
+// Metadata errors of units first, first + stride, ... (a row index outside the
+// batch; a row whose keys need more blocks than the block table holds), each
+// reported by the CTA that owns the row's first unit of a kv head or its last
+// pair. The builder of a unit list checks its rows itself.
+__device__ __forceinline__ void report_unit_errors(const PrefillParams& p, int first, int stride, int units) {
+  if (p.unit_list) return;
+  for (int u = first; u < units; u += stride) {
+    const int prow = (u / p.mpairs) / p.hkv;
+    const int row = p.rows ? __ldg(p.rows + prow) : prow;
+    if (u % (p.mpairs * p.hkv) == 0 && (row < 0 || row >= p.num_rows)) atomic_or_err(p.err, SEB_ERRBIT_META);
+    if (row >= 0 && row < p.num_rows && (u % p.mpairs) == p.mpairs - 1) {
+      const int k_len = max(__ldg(p.k_lens + row), 0);
+      if (((k_len + 15) >> 4) > p.max_blocks && (u / p.mpairs) % p.hkv == 0) atomic_or_err(p.err, SEB_ERRBIT_KLEN);
+    }
+  }
+}
+
 template <typename T, int D>
 __global__ void __launch_bounds__(kThreads, 1)
     prefill_tc_kernel(const PrefillParams p, const __grid_constant__ CUtensorMap tmap_q,
@@ -271,76 +332,21 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int lane = threadIdx.x & 31;
 
   static_assert(D == 64, "TMEM layout for head_dim 64 (O and P's remainder: 64 columns per Q tile)");
-  // ---- work unit: (prefill row, kv head, pair of Q tiles), both Q tiles in
-  // this CTA. Pairs are visited late-first (they are the longest).
-  int bx = blockIdx.x;
-  int pr, kvh, row;
-  if (p.unit_list) {
-    if (bx >= __ldg(p.num_units)) return;
-    row = __ldg(p.unit_list + 2 * bx);
-    const int e = __ldg(p.unit_list + 2 * bx + 1);
-    kvh = e & 255;
-    pr = e >> 8;
-    if (row < 0 || row >= p.num_rows) return;  // the list's builder reports bad rows
-  } else {
-    pr = p.mpairs - 1 - (bx % p.mpairs);
-    bx /= p.mpairs;
-    kvh = bx % p.hkv;
-    const int prow = bx / p.hkv;
-    if (prow >= p.num_prefill_rows) return;
-    row = p.rows ? __ldg(p.rows + prow) : prow;
-    if (row < 0 || row >= p.num_rows) {
-      if (threadIdx.x == 0 && kvh == 0 && pr == 0) atomic_or_err(p.err, SEB_ERRBIT_META);
-      return;
-    }
-  }
-  const int q_len = __ldg(p.q_lens + row);
-  const int q_start = __ldg(p.q_starts + row);
-  const int k_len = max(__ldg(p.k_lens + row), 0);
-  const int qpos0 = __ldg(p.q_pos + row);
-  const int ceil16 = (k_len + 15) & ~15;
-  const int pair0 = pr * kQT * p.qpt;  // first query of the pair
-  if (pair0 >= q_len) return;
-  const bool has_second = pair0 + p.qpt < q_len;
-  const int i0 = pair0;                     // first query of this CTA
-  const int nqt = has_second ? 2 : 1;       // Q tiles of this CTA
-  // P's remainder pass for both Q tiles when the pair's first query sees few keys
-  const bool split = (p.causal ? min(ceil16, qpos0 + i0 + 1) : ceil16) < kSplitBelow;
-  const int i_last = min(i0 + nqt * p.qpt, q_len) - 1;
-  int nvis_tile = p.causal ? min(ceil16, qpos0 + i_last + 1) : ceil16;
-  nvis_tile = max(nvis_tile, 0);
-  int nblk = (nvis_tile + 15) >> 4;
-  if (nblk > p.max_blocks) {
-    if (threadIdx.x == 0) atomic_or_err(p.err, SEB_ERRBIT_KLEN);
-    nblk = (int)p.max_blocks;
-    nvis_tile = nblk * 16;
-  }
-  const int ntiles = (nblk + 7) >> 3;
+  // Persistent: CTA c walks the work units c, c + gridDim.x, ... with its Q
+  // buffers, K/V rings and barrier phases running on from unit to unit, so the
+  // next unit's Q and first K/V tiles load while the current unit finishes.
+  // Every thread reads the same unit count, so all roles walk the same units.
+  const int units = p.unit_list ? min(__ldg(p.num_units), p.unit_cap) : p.num_prefill_rows * p.hkv * p.mpairs;
   const int G = p.group;
-
-  // Softmax-thread identity: warpgroup `qt` owns Q tile qt; a thread owns one
-  // MMA row (TMEM lane) m = query (m / G), head (m % G).
-  const int qt = (warp - 2) >> 2;
-  const int q4 = warp & 3;
-  const int m = q4 * 32 + lane;
-  const int qi = i0 + qt * p.qpt + m / G;
-  const int gh = m % G;
-  const bool row_valid = (warp >= 2) && qt < nqt && qi <= i_last;
-
-  if (ntiles == 0) {
-    // No visible keys: the reference's loop never runs, O = 0/0, LSE = -inf.
-    if (row_valid) {
-      T* op = reinterpret_cast<T*>(p.out) + (int64_t)(q_start + qi) * p.o_st + (int64_t)(kvh * G + gh) * p.o_sh;
-      for (int d = 0; d < D; ++d) op[d] = Elem<T>::from_float(__int_as_float(0x7fc00000));
-      p.lse[(int64_t)(q_start + qi) * p.lse_st + kvh * G + gh] = -INFINITY;
-    }
-    return;
-  }
+  if (threadIdx.x == 0) report_unit_errors(p, blockIdx.x, gridDim.x, units);
 
   const uint32_t bar = base + L::oBar;  // mbarrier i at bar + 8 * i
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sbase + L::oBar + 8 * kNumBars);
   if (threadIdx.x == 0) {
-    mbar_init(bar + 8 * kBarQ, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(bar + 8 * (kBarQFull + b), 1);
+      mbar_init(bar + 8 * (kBarQEmpty + b), 1);
+    }
     for (int s = 0; s < kKStages; ++s) {
       mbar_init(bar + 8 * (kBarKFull + s), 1);
       mbar_init(bar + 8 * (kBarKEmpty + s), 1);
@@ -352,8 +358,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int t = 0; t < kQT; ++t) {
       mbar_init(bar + 8 * (kBarSFull + t), 1);
       mbar_init(bar + 8 * (kBarPFull + t), 4);
+      mbar_init(bar + 8 * (kBarODone + t), 1);
     }
-    mbar_init(bar + 8 * kBarDone, 1);
+    mbar_init(bar + 8 * kBarFinal, 1);
     fence_mbar_init();
   }
   if (warp == 1) {
@@ -365,6 +372,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc::fence_after_sync();
   const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(tmem_slot);
   bool failed = false;
+  PairUnit w;
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -372,79 +380,93 @@ __global__ void __launch_bounds__(kThreads, 1)
       prefetch_tensor_map(&tmap_q);
       prefetch_tensor_map(&tmap_k);
       prefetch_tensor_map(&tmap_v);
-      mbar_arrive_expect_tx(bar + 8 * kBarQ, nqt * L::kTileQ);
-      for (int t = 0; t < nqt; ++t)
-#pragma unroll
-        for (int pn = 0; pn < L::kPanels; ++pn)
-          tma_load_3d(base + L::oQ + t * L::kTileQ + pn * L::kPanel, &tmap_q, pn * 64, kvh * G,
-                      q_start + i0 + t * p.qpt, bar + 8 * kBarQ);
     }
-    const int32_t* bt = p.block_table + (int64_t)row * p.bt_stride;
-    // Block ids are read a window of 4 tiles (32 blocks, one per lane) ahead of
-    // their use, so the copies never wait on a block-table load. K and V keep
-    // their own windows.
-    auto fetch = [&](int w) -> int {
-      const int blk = 32 * w + lane;
-      return blk < nblk ? __ldg(bt + blk) : 0;
-    };
-    int kcur = fetch(0), knext = fetch(1), kw = 0;
-    int vcur = kcur, vnext = knext, vw = 0;
-    auto block_id = [&](int t, int& cur, int& next, int& w) -> int {
-      while (w < (t >> 2)) {
-        cur = next;
-        next = fetch(w + 2);
-        ++w;
-      }
-      return __shfl_sync(kFullMask, cur, ((t & 3) << 3) + (lane & 7));
-    };
-    // Load K (is_v = 0) or V (is_v = 1) of tile j (8 blocks) into its ring stage.
-    auto load = [&](int j, int is_v) -> bool {
-      const int stages = is_v ? kVStages : kKStages;
-      const int s = j % stages;
-      const int u = j / stages;
-      int bid = is_v ? block_id(j, vcur, vnext, vw) : block_id(j, kcur, knext, kw);
-      if (u >= 1 && !wait_or_flag(bar + 8 * ((is_v ? kBarVEmpty : kBarKEmpty) + s), (u - 1) & 1, failed))
-        return false;
-      const int nb = min(8, nblk - 8 * j);
-      if (lane < nb && (bid < 0 || (int64_t)bid >= p.num_blocks)) {
-        atomic_or_err(p.err, SEB_ERRBIT_BLOCK_ID);
-        bid = 0;  // read a real block instead; the row's result is flagged as invalid
-      }
-      const uint32_t fb = bar + 8 * ((is_v ? kBarVFull : kBarKFull) + s);
-      if (lane == 0) mbar_arrive_expect_tx(fb, nb * L::kPanels * 2048);
-      __syncwarp();
-      if (lane < nb) {
-        const uint32_t dst = base + (is_v ? L::oV : L::oK) + s * L::kTileKV + lane * 2048;
+    int gk = 0, gv = 0;  // K and V tiles loaded so far (ring positions)
+    int nq = 0;          // units whose Q was loaded so far (Q buffer nq & 1)
+    for (int u = blockIdx.x; u < units && !failed; u += gridDim.x) {
+      if (!pair_unit(p, u, w) || w.ntiles == 0) continue;
+      const int nqt = w.pair0 + p.qpt < w.q_len ? 2 : 1;  // Q tiles of the unit
+      // Q into buffer nq & 1 once the S MMAs of the unit two back have read it.
+      const int qb = nq & 1;
+      if (nq >= 2 && !wait_or_flag(bar + 8 * (kBarQEmpty + qb), ((nq >> 1) - 1) & 1, failed)) break;
+      if (lane == 0) {
+        mbar_arrive_expect_tx(bar + 8 * (kBarQFull + qb), nqt * L::kTileQ);
+        for (int t = 0; t < nqt; ++t)
 #pragma unroll
-        for (int pn = 0; pn < L::kPanels; ++pn)
-          tma_load_3d(dst + pn * L::kPanel, is_v ? &tmap_v : &tmap_k, pn * 64, kvh, bid * 16, fb);
+          for (int pn = 0; pn < L::kPanels; ++pn)
+            tma_load_3d(base + L::oQ + (qb * kQT + t) * L::kTileQ + pn * L::kPanel, &tmap_q, pn * 64, w.kvh * G,
+                        w.q_start + w.pair0 + t * p.qpt, bar + 8 * (kBarQFull + qb));
       }
-      return true;
-    };
-    // The MMA warp consumes K(0), then per tile j V(j) and K(j+1).
-    int k_issued = 0, v_issued = 0;
-    for (int j = 0; j < ntiles && !failed; ++j) {
-      if (load(j, 0)) ++k_issued;
-      if (load(j, 1)) ++v_issued;
+      __syncwarp();
+      ++nq;
+      const int32_t* bt = p.block_table + (int64_t)w.row * p.bt_stride;
+      const int nblk = w.nblk;
+      // Block ids are read a window of 4 tiles (32 blocks, one per lane) ahead of
+      // their use, so the copies never wait on a block-table load. K and V keep
+      // their own windows.
+      auto fetch = [&](int win) -> int {
+        const int blk = 32 * win + lane;
+        return blk < nblk ? __ldg(bt + blk) : 0;
+      };
+      int kcur = fetch(0), knext = fetch(1), kw = 0;
+      int vcur = kcur, vnext = knext, vw = 0;
+      auto block_id = [&](int t, int& cur, int& next, int& win) -> int {
+        while (win < (t >> 2)) {
+          cur = next;
+          next = fetch(win + 2);
+          ++win;
+        }
+        return __shfl_sync(kFullMask, cur, ((t & 3) << 3) + (lane & 7));
+      };
+      // Load K (is_v = 0) or V (is_v = 1) of tile j (8 blocks) into its ring stage.
+      auto load = [&](int j, int is_v) -> bool {
+        const int stages = is_v ? kVStages : kKStages;
+        const int g = is_v ? gv : gk;
+        const int s = g % stages;
+        const int uu = g / stages;
+        int bid = is_v ? block_id(j, vcur, vnext, vw) : block_id(j, kcur, knext, kw);
+        if (uu >= 1 && !wait_or_flag(bar + 8 * ((is_v ? kBarVEmpty : kBarKEmpty) + s), (uu - 1) & 1, failed))
+          return false;
+        const int nb = min(8, nblk - 8 * j);
+        if (lane < nb && (bid < 0 || (int64_t)bid >= p.num_blocks)) {
+          atomic_or_err(p.err, SEB_ERRBIT_BLOCK_ID);
+          bid = 0;  // read a real block instead; the row's result is flagged as invalid
+        }
+        const uint32_t fb = bar + 8 * ((is_v ? kBarVFull : kBarKFull) + s);
+        if (lane == 0) mbar_arrive_expect_tx(fb, nb * L::kPanels * 2048);
+        __syncwarp();
+        if (lane < nb) {
+          const uint32_t dst = base + (is_v ? L::oV : L::oK) + s * L::kTileKV + lane * 2048;
+#pragma unroll
+          for (int pn = 0; pn < L::kPanels; ++pn)
+            tma_load_3d(dst + pn * L::kPanel, is_v ? &tmap_v : &tmap_k, pn * 64, w.kvh, bid * 16, fb);
+        }
+        if (is_v) ++gv;
+        else ++gk;
+        return true;
+      };
+      // The MMA warp consumes K(0), then per tile j V(j) and K(j+1).
+      for (int j = 0; j < w.ntiles; ++j)
+        if (!load(j, 0) || !load(j, 1)) break;
     }
     // Leave no copy in flight: the last loads must have landed.
-    for (int j = max(0, k_issued - kKStages); j < k_issued; ++j)
-      mbar_wait_bounded(bar + 8 * (kBarKFull + j % kKStages), (j / kKStages) & 1, 1u << 16);
-    for (int j = max(0, v_issued - kVStages); j < v_issued; ++j)
-      mbar_wait_bounded(bar + 8 * (kBarVFull + j % kVStages), (j / kVStages) & 1, 1u << 16);
+    for (int i = max(0, nq - 2); i < nq; ++i)
+      mbar_wait_bounded(bar + 8 * (kBarQFull + (i & 1)), (i >> 1) & 1, 1u << 16);
+    for (int i = max(0, gk - kKStages); i < gk; ++i)
+      mbar_wait_bounded(bar + 8 * (kBarKFull + i % kKStages), (i / kKStages) & 1, 1u << 16);
+    for (int i = max(0, gv - kVStages); i < gv; ++i)
+      mbar_wait_bounded(bar + 8 * (kBarVFull + i % kVStages), (i / kVStages) & 1, 1u << 16);
   } else if (warp == 1) {
     // ---------------------------------------------------------------- MMA
     constexpr uint32_t idesc_qk = tc::idesc_f16(kBf16, false, kBM, kBN);
     constexpr uint32_t idesc_pv = tc::idesc_f16(kBf16, true, kBM, D);
-    wait_or_flag(bar + 8 * kBarQ, 0, failed);
-    // S(t, j) = Q(t) K(j)^T into the S/P columns of Q tile t.
-    auto issue_s = [&](int t, int j) {
-      const int s = j % kKStages;
+    // S(t) = Q(t) K^T from Q buffer qb and K stage s into the S/P columns of Q tile t.
+    auto issue_s = [&](int t, int qb, int s) {
       if (lane == 0) {
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint64_t a = tc::smem_desc_sw128(
-              base + L::oQ + t * L::kTileQ + (kk >> 2) * L::kPanel + (kk & 3) * 32, 16, 1024);
+              base + L::oQ + (qb * kQT + t) * L::kTileQ + (kk >> 2) * L::kPanel + (kk & 3) * 32, 16, 1024);
           const uint64_t bd = tc::smem_desc_sw128(
               base + L::oK + s * L::kTileKV + (kk >> 2) * L::kPanel + (kk & 3) * 32, 16, 1024);
           tc::mma_ss(tmem + kColS + t * 128, a, bd, idesc_qk, kk > 0);
@@ -453,14 +475,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       __syncwarp();
     };
-    // O(t) += P(t, j) V(j), P read from TMEM.
-    auto issue_pv = [&](int t, int j) {
-      const int s = j % kVStages;
+    // O(t) += P(t) V from V stage s, P read from TMEM (first: O(t) = P(t) V).
+    auto issue_pv = [&](int t, int s, bool first, bool split) {
       if (lane == 0) {
 #pragma unroll
         for (int kk = 0; kk < kBN / 16; ++kk) {
           const uint64_t bd = tc::smem_desc_sw128(base + L::oV + s * L::kTileKV + kk * 2048, L::kPanel, 1024);
-          tc::mma_ts(tmem + kColO + t * D, tmem + kColS + t * 128 + 8 * kk, bd, idesc_pv, j > 0 || kk > 0);
+          tc::mma_ts(tmem + kColO + t * D, tmem + kColS + t * 128 + 8 * kk, bd, idesc_pv, !first || kk > 0);
         }
         if (split) {  // P's remainder, from its own columns
 #pragma unroll
@@ -472,160 +493,214 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       __syncwarp();
     };
+    int gk = 0, gv = 0, nq = 0;
+    uint32_t pphase = 0;  // bit t: parity of Q tile t's next P arrival
     // Ping-pong: per KV tile j and Q tile t, PV(t, j) then S(t, j+1), so one Q
     // tile's softmax runs while the other tile's MMAs execute. S(t, j+1)
     // overwrites the columns PV(t, j) reads P from; both are issued by this one
     // thread, and the tensor pipe runs one thread's MMAs in issue order, so
     // S(t, j+1) follows PV(t, j) at once (no wait for PV(t, j) to complete).
-    if (wait_or_flag(bar + 8 * kBarKFull, 0, failed)) {
-      for (int t = 0; t < nqt; ++t) issue_s(t, 0);
-      if (lane == 0) tc::commit(bar + 8 * kBarKEmpty);
-      __syncwarp();
-    }
-    for (int j = 0; j < ntiles && !failed; ++j) {
-      const int sv = j % kVStages;
-      if (!wait_or_flag(bar + 8 * (kBarVFull + sv), (j / kVStages) & 1, failed)) break;
-      // Rows of this tile that hold real keys: loaded (nblk) and below k_len.
-      const int r0 = min(max(k_len - j * kBN, 0), min(8, nblk - 8 * j) * 16);
-      if (r0 < kBN) {
-        // V rows of padding keys must be exact zeros (their P is 0 or, for the
-        // reference's zero-padded keys, exp(-m)); the pool past k_len and the
-        // rows of blocks this tile did not load may hold anything.
-        char* vt = sbase + L::oV + sv * L::kTileKV;
-        for (int c = lane; c < (kBN - r0) * L::kPanels * 8; c += 32) {
-          const int r = r0 + c / (L::kPanels * 8);
-          const int rem = c % (L::kPanels * 8);
-          *reinterpret_cast<uint4*>(vt + (rem >> 3) * L::kPanel + r * 128 + (rem & 7) * 16) = make_uint4(0, 0, 0, 0);
+    // The same holds across units: the next unit's S(t, 0) follows this unit's
+    // last PV(t, j), and its PV(t, 0), which overwrites O(t), waits for the
+    // tile's P arrival, which the softmax posts after it read O(t).
+    for (int u = blockIdx.x; u < units && !failed; u += gridDim.x) {
+      if (!pair_unit(p, u, w) || w.ntiles == 0) continue;
+      const int nqt = w.pair0 + p.qpt < w.q_len ? 2 : 1;
+      const int qb = nq & 1;
+      if (!wait_or_flag(bar + 8 * (kBarQFull + qb), (nq >> 1) & 1, failed)) break;
+      ++nq;
+      {
+        const int sk = gk % kKStages;
+        if (!wait_or_flag(bar + 8 * (kBarKFull + sk), (gk / kKStages) & 1, failed)) break;
+        tc::fence_after_sync();
+        for (int t = 0; t < nqt; ++t) issue_s(t, qb, sk);
+        if (lane == 0) {
+          tc::commit(bar + 8 * (kBarKEmpty + sk));
+          if (w.ntiles == 1) tc::commit(bar + 8 * (kBarQEmpty + qb));
         }
-        fence_proxy_async_smem();
         __syncwarp();
+        ++gk;
       }
-      const bool next = j + 1 < ntiles;
-      const int sk = (j + 1) % kKStages;
-      for (int t = 0; t < nqt && !failed; ++t) {
-        if (!wait_or_flag(bar + 8 * (kBarPFull + t), j & 1, failed)) break;
-        tc::fence_after_sync();
-        issue_pv(t, j);
-        if (!next) continue;
-        if (t == 0 && !wait_or_flag(bar + 8 * (kBarKFull + sk), ((j + 1) / kKStages) & 1, failed)) break;
-        tc::fence_after_sync();
-        issue_s(t, j + 1);
+      for (int j = 0; j < w.ntiles && !failed; ++j) {
+        const int sv = gv % kVStages;
+        if (!wait_or_flag(bar + 8 * (kBarVFull + sv), (gv / kVStages) & 1, failed)) break;
+        // Rows of this tile that hold real keys: loaded (nblk) and below k_len.
+        const int r0 = min(max(w.k_len - j * kBN, 0), min(8, w.nblk - 8 * j) * 16);
+        if (r0 < kBN) {
+          // V rows of padding keys must be exact zeros (their P is 0 or, for the
+          // reference's zero-padded keys, exp(-m)); the pool past k_len and the
+          // rows of blocks this tile did not load may hold anything.
+          char* vt = sbase + L::oV + sv * L::kTileKV;
+          for (int c = lane; c < (kBN - r0) * L::kPanels * 8; c += 32) {
+            const int r = r0 + c / (L::kPanels * 8);
+            const int rem = c % (L::kPanels * 8);
+            *reinterpret_cast<uint4*>(vt + (rem >> 3) * L::kPanel + r * 128 + (rem & 7) * 16) = make_uint4(0, 0, 0, 0);
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+        }
+        const bool next = j + 1 < w.ntiles;
+        const int sk = gk % kKStages;
+        for (int t = 0; t < nqt && !failed; ++t) {
+          if (!wait_or_flag(bar + 8 * (kBarPFull + t), (pphase >> t) & 1u, failed)) break;
+          pphase ^= 1u << t;
+          tc::fence_after_sync();
+          issue_pv(t, sv, j == 0, w.split);
+          if (!next) {
+            if (lane == 0) tc::commit(bar + 8 * (kBarODone + t));
+            __syncwarp();
+            continue;
+          }
+          if (t == 0 && !wait_or_flag(bar + 8 * (kBarKFull + sk), (gk / kKStages) & 1, failed)) break;
+          tc::fence_after_sync();
+          issue_s(t, qb, sk);
+        }
+        if (lane == 0) {
+          tc::commit(bar + 8 * (kBarVEmpty + sv));
+          if (next) {
+            tc::commit(bar + 8 * (kBarKEmpty + sk));
+            if (j + 2 == w.ntiles) tc::commit(bar + 8 * (kBarQEmpty + qb));
+          }
+        }
+        __syncwarp();
+        ++gv;
+        if (next) ++gk;
       }
-      if (lane == 0) {
-        tc::commit(bar + 8 * (kBarVEmpty + sv));
-        if (next) tc::commit(bar + 8 * (kBarKEmpty + sk));
-      }
-      __syncwarp();
     }
     // Every MMA this thread issued has completed before TMEM is released.
-    if (lane == 0) tc::commit(bar + 8 * kBarDone);
+    if (lane == 0) tc::commit(bar + 8 * kBarFinal);
     __syncwarp();
-    mbar_wait_bounded(bar + 8 * kBarDone, 0, 1u << 20);
-  } else if (qt < nqt) {
+    mbar_wait_bounded(bar + 8 * kBarFinal, 0, 1u << 20);
+  } else {
     // ------------------------------------------------------------ softmax
+    // Warpgroup qt owns Q tile qt of every unit that has it; a thread owns one
+    // MMA row (TMEM lane) m = query (m / G), head (m % G).
+    const int qt = (warp - 2) >> 2;
+    const int q4 = warp & 3;
+    const int m = q4 * 32 + lane;
     const uint32_t taddr = tmem + ((uint32_t)(q4 * 32) << 16);
     const uint32_t col_s = kColS + qt * 128;
     const uint32_t col_o = kColO + qt * D;
-    const int pos = qpos0 + qi;
-    const int vis = row_valid ? (p.causal ? min(ceil16, pos + 1) : ceil16) : 0;
-    const int min_vis = p.causal ? min(ceil16, qpos0 + i0 + qt * p.qpt + 1) : ceil16;
     const float c = p.scale_log2;
-    float m_ref = -INFINITY;
-    float l = 0.f;
-    // After a failed (timed-out) wait the loop keeps its shape with the waits
-    // skipped; warp-collective TMEM accesses stay warp-uniform.
-    for (int j = 0; j < ntiles; ++j) {
-      // S(t, j) complete; its commit also covers PV(t, j-1), so O is stable.
-      wait_or_flag(bar + 8 * (kBarSFull + qt), j & 1, failed);
-      tc::fence_after_sync();
-      // Tiles every valid row of the Q tile sees in full need no mask: scores
-      // stay raw and the (positive) scale folds into the row max and the
-      // exponent's FMA. Any other scale takes the masked path, which scales first.
-      const bool full = c > 0.f && (j + 1) * kBN <= min_vis && (j + 1) * kBN <= k_len;
-      const float cm = full ? c : 1.f;
-      // The row's 128 scores in one TMEM round trip.
-      float x[4][32];
-#pragma unroll
-      for (int ch = 0; ch < 4; ++ch) tc::tmem_ld32(taddr + col_s + 32 * ch, x[ch]);
-      tc::tmem_wait_ld();
-      if (!full) {
-#pragma unroll
-        for (int ch = 0; ch < 4; ++ch) mask_chunk(x[ch], j * kBN + 32 * ch, vis, k_len, c);
-      }
-      float mx[8];
-#pragma unroll
-      for (int i = 0; i < 8; ++i) mx[i] = fmaxf(fmaxf(x[0][i], x[0][8 + i]), fmaxf(x[0][16 + i], x[0][24 + i]));
-#pragma unroll
-      for (int ch = 1; ch < 4; ++ch)
-#pragma unroll
-        for (int i = 0; i < 8; ++i)
-          mx[i] = fmaxf(mx[i], fmaxf(fmaxf(x[ch][i], x[ch][8 + i]), fmaxf(x[ch][16 + i], x[ch][24 + i])));
-      const float mb =
-          cm * fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])), fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
-      const bool need = mb > m_ref + kLazyThreshold;
-      float factor = 1.f;
-      if (need) {
-        factor = fast_exp2(m_ref - mb);  // 0 while m_ref is -inf
-        l *= factor;
-        m_ref = mb;
-      }
-      // P = 2^(s - m) as 16-bit pairs over the first 64 S columns (already read),
-      // its remainder (split pairs) in the tile's remainder columns.
-      const float neg_m = m_ref == -INFINITY ? 0.f : -m_ref;
-      float ls[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-      for (int ch = 0; ch < 4; ++ch) {
-        {
-          uint32_t hi[16];
-#pragma unroll
-          for (int e = 0; e < 16; ++e) {
-            const float a0 = fast_exp2(fmaf(x[ch][2 * e], cm, neg_m));
-            const float a1 = fast_exp2(fmaf(x[ch][2 * e + 1], cm, neg_m));
-            ls[e & 3] += a0 + a1;
-            hi[e] = Mma<T>::pack(a0, a1);
-            x[ch][2 * e] = a0;  // probabilities replace the consumed scores
-            x[ch][2 * e + 1] = a1;
-          }
-          tc::tmem_st16u(taddr + col_s + 16 * ch, hi);
+    int ns = 0;  // S tiles of Q tile qt consumed so far (parity of kBarSFull + qt)
+    int nu = 0;  // units of Q tile qt finished so far (parity of kBarODone + qt)
+    for (int u = blockIdx.x; u < units; u += gridDim.x) {
+      if (!pair_unit(p, u, w)) continue;
+      const int nqt = w.pair0 + p.qpt < w.q_len ? 2 : 1;
+      if (qt >= nqt) continue;
+      const int i0 = w.pair0 + qt * p.qpt;  // first query of this Q tile
+      const int qi = i0 + m / G;
+      const int gh = m % G;
+      const bool row_valid = qi <= w.i_last;
+      T* op = reinterpret_cast<T*>(p.out) + (int64_t)(w.q_start + qi) * p.o_st + (int64_t)(w.kvh * G + gh) * p.o_sh;
+      float* lp = p.lse + (int64_t)(w.q_start + qi) * p.lse_st + w.kvh * G + gh;
+      if (w.ntiles == 0) {
+        // No visible keys: the reference's loop never runs, O = 0/0, LSE = -inf.
+        if (row_valid) {
+          for (int d = 0; d < D; ++d) op[d] = Elem<T>::from_float(__int_as_float(0x7fc00000));
+          *lp = -INFINITY;
         }
-        if (split) {  // remainder p - round16(p), recomputed from the probabilities
-          uint32_t lo[16];
-#pragma unroll
-          for (int e = 0; e < 16; ++e) {
-            const float2 f = Mma<T>::unpack(Mma<T>::pack(x[ch][2 * e], x[ch][2 * e + 1]));
-            lo[e] = Mma<T>::pack(x[ch][2 * e] - f.x, x[ch][2 * e + 1] - f.y);
-          }
-          tc::tmem_st16u(taddr + kColRem + qt * 64 + 16 * ch, lo);
-        }
+        continue;
       }
-      l += (ls[0] + ls[1]) + (ls[2] + ls[3]);
-      // O is stable (the S commit covers PV(t, j-1)); PV(t, j) is issued only
-      // after this thread's P arrival, so the rescale may come last.
-      if (j > 0 && __any_sync(kFullMask, need)) {
-        // warp-collective: rows that keep their reference max scale by 1
+      const int pos = w.qpos0 + qi;
+      const int vis = row_valid ? (p.causal ? min(w.ceil16, pos + 1) : w.ceil16) : 0;
+      const int min_vis = p.causal ? min(w.ceil16, w.qpos0 + i0 + 1) : w.ceil16;
+      float m_ref = -INFINITY;
+      float l = 0.f;
+      // After a failed (timed-out) wait the loop keeps its shape with the waits
+      // skipped; warp-collective TMEM accesses stay warp-uniform.
+      for (int j = 0; j < w.ntiles; ++j, ++ns) {
+        // S(t, j) complete; its commit also covers PV(t, j-1), so O is stable.
+        wait_or_flag(bar + 8 * (kBarSFull + qt), ns & 1, failed);
+        tc::fence_after_sync();
+        // Tiles every valid row of the Q tile sees in full need no mask: scores
+        // stay raw and the (positive) scale folds into the row max and the
+        // exponent's FMA. Any other scale takes the masked path, which scales first.
+        const bool full = c > 0.f && (j + 1) * kBN <= min_vis && (j + 1) * kBN <= w.k_len;
+        const float cm = full ? c : 1.f;
+        // The row's 128 scores in one TMEM round trip.
+        float x[4][32];
+#pragma unroll
+        for (int ch = 0; ch < 4; ++ch) tc::tmem_ld32(taddr + col_s + 32 * ch, x[ch]);
+        tc::tmem_wait_ld();
+        if (!full) {
+#pragma unroll
+          for (int ch = 0; ch < 4; ++ch) mask_chunk(x[ch], j * kBN + 32 * ch, vis, w.k_len, c);
+        }
+        float mx[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) mx[i] = fmaxf(fmaxf(x[0][i], x[0][8 + i]), fmaxf(x[0][16 + i], x[0][24 + i]));
+#pragma unroll
+        for (int ch = 1; ch < 4; ++ch)
+#pragma unroll
+          for (int i = 0; i < 8; ++i)
+            mx[i] = fmaxf(mx[i], fmaxf(fmaxf(x[ch][i], x[ch][8 + i]), fmaxf(x[ch][16 + i], x[ch][24 + i])));
+        const float mb =
+            cm * fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])), fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
+        const bool need = mb > m_ref + kLazyThreshold;
+        float factor = 1.f;
+        if (need) {
+          factor = fast_exp2(m_ref - mb);  // 0 while m_ref is -inf
+          l *= factor;
+          m_ref = mb;
+        }
+        // P = 2^(s - m) as 16-bit pairs over the first 64 S columns (already read),
+        // its remainder (split pairs) in the tile's remainder columns.
+        const float neg_m = m_ref == -INFINITY ? 0.f : -m_ref;
+        float ls[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int ch = 0; ch < 4; ++ch) {
+          {
+            uint32_t hi[16];
+#pragma unroll
+            for (int e = 0; e < 16; ++e) {
+              const float a0 = fast_exp2(fmaf(x[ch][2 * e], cm, neg_m));
+              const float a1 = fast_exp2(fmaf(x[ch][2 * e + 1], cm, neg_m));
+              ls[e & 3] += a0 + a1;
+              hi[e] = Mma<T>::pack(a0, a1);
+              x[ch][2 * e] = a0;  // probabilities replace the consumed scores
+              x[ch][2 * e + 1] = a1;
+            }
+            tc::tmem_st16u(taddr + col_s + 16 * ch, hi);
+          }
+          if (w.split) {  // remainder p - round16(p), recomputed from the probabilities
+            uint32_t lo[16];
+#pragma unroll
+            for (int e = 0; e < 16; ++e) {
+              const float2 f = Mma<T>::unpack(Mma<T>::pack(x[ch][2 * e], x[ch][2 * e + 1]));
+              lo[e] = Mma<T>::pack(x[ch][2 * e] - f.x, x[ch][2 * e + 1] - f.y);
+            }
+            tc::tmem_st16u(taddr + kColRem + qt * 64 + 16 * ch, lo);
+          }
+        }
+        l += (ls[0] + ls[1]) + (ls[2] + ls[3]);
+        // O is stable (the S commit covers PV(t, j-1)); PV(t, j) is issued only
+        // after this thread's P arrival, so the rescale may come last.
+        if (j > 0 && __any_sync(kFullMask, need)) {
+          // warp-collective: rows that keep their reference max scale by 1
 #pragma unroll 1
-        for (int cc = 0; cc < D / 16; ++cc) {
-          float o[16];
-          const uint32_t a = taddr + col_o + 16 * cc;
-          tc::tmem_ld16(a, o);
-          tc::tmem_wait_ld();
+          for (int cc = 0; cc < D / 16; ++cc) {
+            float o[16];
+            const uint32_t a = taddr + col_o + 16 * cc;
+            tc::tmem_ld16(a, o);
+            tc::tmem_wait_ld();
 #pragma unroll
-          for (int i = 0; i < 16; ++i) o[i] *= factor;
-          tc::tmem_st16(a, o);
+            for (int i = 0; i < 16; ++i) o[i] *= factor;
+            tc::tmem_st16(a, o);
+          }
         }
+        tc::tmem_wait_st();
+        tc::fence_before_sync();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar + 8 * (kBarPFull + qt));
       }
-      tc::tmem_wait_st();
-      tc::fence_before_sync();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(bar + 8 * (kBarPFull + qt));
-    }
-    // ------------------------------------------------------------ epilogue
-    // Every MMA, the last PV of this Q tile included, has completed.
-    wait_or_flag(bar + 8 * kBarDone, 0, failed);
-    tc::fence_after_sync();
-    if (!__any_sync(kFullMask, failed)) {  // warp-uniform: tcgen05.ld is warp-collective
+      // ---------------------------------------------------------- epilogue
+      // The unit's last PV of this Q tile has completed: O is final.
+      wait_or_flag(bar + 8 * (kBarODone + qt), nu & 1, failed);
+      ++nu;
+      tc::fence_after_sync();
+      if (__any_sync(kFullMask, failed)) break;  // warp-uniform: tcgen05.ld is warp-collective
       const float inv = 1.f / l;
-      T* op = reinterpret_cast<T*>(p.out) + (int64_t)(q_start + qi) * p.o_st + (int64_t)(kvh * G + gh) * p.o_sh;
 #pragma unroll
       for (int cc = 0; cc < D / 32; ++cc) {
         float o[32];
@@ -634,14 +709,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (row_valid) {
 #pragma unroll
           for (int v8 = 0; v8 < 4; ++v8) {
-            uint32_t w[4];
+            uint32_t wv[4];
 #pragma unroll
-            for (int e = 0; e < 4; ++e) w[e] = Mma<T>::pack(o[8 * v8 + 2 * e] * inv, o[8 * v8 + 2 * e + 1] * inv);
-            *reinterpret_cast<uint4*>(op + 32 * cc + 8 * v8) = make_uint4(w[0], w[1], w[2], w[3]);
+            for (int e = 0; e < 4; ++e) wv[e] = Mma<T>::pack(o[8 * v8 + 2 * e] * inv, o[8 * v8 + 2 * e + 1] * inv);
+            *reinterpret_cast<uint4*>(op + 32 * cc + 8 * v8) = make_uint4(wv[0], wv[1], wv[2], wv[3]);
           }
         }
       }
-      if (row_valid) p.lse[(int64_t)(q_start + qi) * p.lse_st + kvh * G + gh] = m_ref * kLn2p + logf(l);
+      if (row_valid) *lp = m_ref * kLn2p + logf(l);
+      // The next unit's first PV overwrites O: order this warp's O loads before
+      // its next P arrival.
+      tc::fence_before_sync();
     }
   }
 
@@ -718,44 +796,6 @@ enum {
 };
 static_assert(kPNumBars * 8 + 16 <= 512, "barrier region");
 
-// One work unit of the pair kernel, decoded identically by every role of both CTAs.
-struct PairUnit {
-  int row, kvh, q_len, q_start, k_len, qpos0, ceil16, pair0, i_last, nblk, ntiles;
-  bool split;
-};
-
-// Decodes unit u; false: the unit does nothing (no such row or pair).
-__device__ __forceinline__ bool pair_unit(const PrefillParams& p, int u, PairUnit& w) {
-  int pr;
-  if (p.unit_list) {
-    w.row = __ldg(p.unit_list + 2 * u);
-    const int e = __ldg(p.unit_list + 2 * u + 1);
-    w.kvh = e & 255;
-    pr = e >> 8;
-  } else {
-    pr = p.mpairs - 1 - (u % p.mpairs);
-    u /= p.mpairs;
-    w.kvh = u % p.hkv;
-    const int prow = u / p.hkv;
-    if (prow >= p.num_prefill_rows) return false;
-    w.row = p.rows ? __ldg(p.rows + prow) : prow;
-  }
-  if (w.row < 0 || w.row >= p.num_rows) return false;
-  w.q_len = __ldg(p.q_lens + w.row);
-  w.q_start = __ldg(p.q_starts + w.row);
-  w.k_len = max(__ldg(p.k_lens + w.row), 0);
-  w.qpos0 = __ldg(p.q_pos + w.row);
-  w.ceil16 = (w.k_len + 15) & ~15;
-  w.pair0 = pr * 2 * p.qpt;
-  if (w.pair0 >= w.q_len) return false;
-  w.i_last = min(w.pair0 + 2 * p.qpt, w.q_len) - 1;
-  w.split = (p.causal ? min(w.ceil16, w.qpos0 + w.pair0 + 1) : w.ceil16) < kSplitBelow;
-  const int nvis = max(p.causal ? min(w.ceil16, w.qpos0 + w.i_last + 1) : w.ceil16, 0);
-  w.nblk = min((nvis + 15) >> 4, (int)p.max_blocks);
-  w.ntiles = (w.nblk + 7) >> 3;
-  return true;
-}
-
 template <typename T>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
     prefill_pair_kernel(const PrefillParams p, const __grid_constant__ CUtensorMap tmap_q,
@@ -778,19 +818,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
   const int units = p.unit_list ? min(__ldg(p.num_units), p.unit_cap) : p.num_prefill_rows * p.hkv * p.mpairs;
   const int G = p.group;
 
-  // Metadata errors are reported once, by the cluster that owns the unit (the
-  // builder of a unit list checks its rows itself).
-  if (threadIdx.x == 0 && crank == 0 && !p.unit_list) {
-    for (int u = cid; u < units; u += nclusters) {
-      const int prow = (u / p.mpairs) / p.hkv;
-      const int row = p.rows ? __ldg(p.rows + prow) : prow;
-      if (u % (p.mpairs * p.hkv) == 0 && (row < 0 || row >= p.num_rows)) atomic_or_err(p.err, SEB_ERRBIT_META);
-      if (row >= 0 && row < p.num_rows && (u % p.mpairs) == p.mpairs - 1) {
-        const int k_len = max(__ldg(p.k_lens + row), 0);
-        if (((k_len + 15) >> 4) > p.max_blocks && (u / p.mpairs) % p.hkv == 0) atomic_or_err(p.err, SEB_ERRBIT_KLEN);
-      }
-    }
-  }
+  // Metadata errors are reported once, by the cluster that owns the unit.
+  if (threadIdx.x == 0 && crank == 0) report_unit_errors(p, cid, nclusters, units);
 
   const uint32_t bar = base + L::oBar;        // this CTA's mbarrier i at bar + 8 i
   const uint32_t lead = mapa_shared(bar, 0);  // the even CTA's
@@ -1282,7 +1311,9 @@ int launch_prefill(const PrefillParams& p, const void* q, int64_t q_st, int64_t 
   if (rc != SEB_OK) return rc;
   rc = kv_tensor_map(&tv, vc, dtype, p.num_blocks, p.hkv, D);
   if (rc != SEB_OK) return rc;
-  const int64_t grid = p.unit_list ? (int64_t)p.unit_cap : (int64_t)p.num_prefill_rows * p.hkv * p.mpairs;
+  // persistent: one CTA per SM (or per unit, when there are fewer)
+  const int64_t units = p.unit_list ? (int64_t)p.unit_cap : (int64_t)p.num_prefill_rows * p.hkv * p.mpairs;
+  const int64_t grid = std::min<int64_t>(units, num_sms());
   kern<<<(unsigned)grid, kThreads, smem, s>>>(p, tq, tk, tv);
   return launch_status("prefill_tc_kernel");
 }
