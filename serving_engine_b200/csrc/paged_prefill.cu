@@ -1388,7 +1388,7 @@ int paged_prefill_impl(const void* q, int64_t q_stride_token, int64_t q_stride_h
   const int64_t grid = unit_list ? (int64_t)unit_cap : (int64_t)num_prefill_rows * num_kv_heads * p.mpairs;
   SEB_CHECK_ARG(grid < (1ll << 31), "seb_paged_prefill: grid too large");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  // head_dim 128: the CTA-pair kernel; head_dim 64: one CTA per pair of Q tiles
+  // head_dim 128: the CTA-pair kernel; head_dim 64: one persistent CTA per SM, a pair of Q tiles per unit
   if (dtype == SEB_BF16) {
     return head_dim == 128 ? launch_prefill_pair<__nv_bfloat16>(p, q, q_stride_token, q_stride_head, total_query,
                                                                 k_cache, v_cache, s)
