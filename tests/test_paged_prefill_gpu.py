@@ -188,6 +188,32 @@ def test_config3_full_size_sampled():
         np.testing.assert_allclose(lse[sl][:, heads].cpu().numpy(), lse_ref[sl][:, heads], atol=1e-3, rtol=0)
 
 
+@pytest.mark.parametrize("d", [64, 128])
+def test_prefill_persistent_walk_vs_oracle(d):
+    """More units than resident CTAs (560 real units of 1,120 named; 148 CTAs at
+    head_dim 64, 74 CTA pairs at 128), so each CTA walks several units with its
+    Q buffers, K/V rings and barrier phases running on from unit to unit: units
+    of one and of two Q tiles, with and without the P-remainder pass, short and
+    long key ranges. The host-split launch and the device router's unit list
+    both match the oracle, and each other bit for bit (a unit's arithmetic does
+    not depend on the CTA that runs it or on what that CTA ran before)."""
+    pattern = [(33, 0), (64, 5), (65, 300), (7, 1500), (130, 0), (200, 64), (96, 1100)]
+    rows = [pattern[i % len(pattern)] for i in range(35)]
+    b = make_batch(rows, 32, 8, d, torch.bfloat16, seed=91 + d)
+    o_ref, lse_ref = oracle(b)
+    o, lse = run_prefill(b)
+    assert_close(o, lse, o_ref, lse_ref, torch.bfloat16)
+    md = metadata_from_lists(b.q_lens, b.k_lens, b.q_starts, b.q_pos_offsets, b.block_tables, DEV)
+    o2, lse2 = paged_flash_attention(b.q.to(DEV), b.k_cache.to(DEV), b.v_cache.to(DEV), md, 32, 8, b.scale)
+    torch.cuda.synchronize()
+    check_device_errors()
+    o2 = o2.float().cpu().numpy()
+    lse2 = lse2.cpu().numpy()
+    assert_close(o2, lse2, o_ref, lse_ref, torch.bfloat16)
+    np.testing.assert_array_equal(o2, o)
+    np.testing.assert_array_equal(lse2, lse)
+
+
 def test_dispatch_mixed_decode_and_prefill_rows():
     """paged_flash_attention sends q_len == 1 rows to the decode kernel and
     q_len > 1 rows to the tcgen05 prefill kernel; together they match the oracle."""
