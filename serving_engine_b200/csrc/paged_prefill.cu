@@ -338,7 +338,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   // Every thread reads the same unit count, so all roles walk the same units.
   const int units = p.unit_list ? min(__ldg(p.num_units), p.unit_cap) : p.num_prefill_rows * p.hkv * p.mpairs;
   const int G = p.group;
-  if (threadIdx.x == 0) report_unit_errors(p, blockIdx.x, gridDim.x, units);
 
   const uint32_t bar = base + L::oBar;  // mbarrier i at bar + 8 * i
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sbase + L::oBar + 8 * kNumBars);
@@ -460,6 +459,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ---------------------------------------------------------------- MMA
     constexpr uint32_t idesc_qk = tc::idesc_f16(kBf16, false, kBM, kBN);
     constexpr uint32_t idesc_pv = tc::idesc_f16(kBf16, true, kBM, D);
+    // Metadata errors of this CTA's units, one unit per lane, while the first
+    // Q and K tiles load.
+    report_unit_errors(p, blockIdx.x + lane * gridDim.x, 32 * gridDim.x, units);
     // S(t) = Q(t) K^T from Q buffer qb and K stage s into the S/P columns of Q tile t.
     auto issue_s = [&](int t, int qb, int s) {
       if (lane == 0) {
@@ -818,8 +820,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
   const int units = p.unit_list ? min(__ldg(p.num_units), p.unit_cap) : p.num_prefill_rows * p.hkv * p.mpairs;
   const int G = p.group;
 
-  // Metadata errors are reported once, by the cluster that owns the unit.
-  if (threadIdx.x == 0 && crank == 0) report_unit_errors(p, cid, nclusters, units);
 
   const uint32_t bar = base + L::oBar;        // this CTA's mbarrier i at bar + 8 i
   const uint32_t lead = mapa_shared(bar, 0);  // the even CTA's
@@ -1036,6 +1036,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
       // Every MMA this warp issued has completed before either CTA releases TMEM.
       if (lane == 0) tc::commit_pair(bar + 8 * kPBarDone, 3);
       __syncwarp();
+    } else if (warp == 1) {
+      // The odd CTA's warp 1 issues nothing: it reports the metadata errors of
+      // the pair's units, one unit per lane, once per unit.
+      report_unit_errors(p, cid + lane * nclusters, 32 * nclusters, units);
     }
     bool done_failed = false;
     wait_or_flag_cluster(bar + 8 * kPBarDone, 0, done_failed);

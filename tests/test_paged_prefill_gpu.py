@@ -214,6 +214,36 @@ def test_prefill_persistent_walk_vs_oracle(d):
     np.testing.assert_array_equal(lse2, lse)
 
 
+@pytest.mark.parametrize("d", [64, 128])
+@pytest.mark.parametrize("fault", ["k_len", "row"])
+def test_prefill_metadata_errors_reported_without_fault(d, fault):
+    """Host-split launches check their metadata on the device, beside the first
+    loads: a k_len needing more blocks than its block-table row holds sets the
+    k_len bit, a listed row index outside the batch the index bit. Nothing
+    faults, and the rows with good metadata match the oracle."""
+    rows = [(70, 0), (33, 100), (128, 37)]
+    b = make_batch(rows, 32, 8, d, torch.bfloat16, seed=5 + d)
+    o_ref, lse_ref = oracle(b)
+    md = metadata_from_lists(b.q_lens, b.k_lens, b.q_starts, b.q_pos_offsets, b.block_tables, DEV)
+    k_lens = md["k_lens"].clone()
+    listed = None
+    if fault == "k_len":
+        # one block past row 0's table row; its causal queries see none of it
+        k_lens[0] = 16 * md["block_table"].shape[1] + 16
+        match = "k_len exceeds block table row"
+    else:
+        listed = torch.tensor([1, 2, 7], dtype=torch.int32, device=DEV)  # row 7 is not in the batch
+        match = "row/query index out of range"
+    o, lse = ops.paged_prefill(b.q.to(DEV), b.k_cache.to(DEV), b.v_cache.to(DEV), md["block_table"], md["q_starts"],
+                               md["q_lens"], k_lens, md["q_pos_offsets"], 32, 8, b.scale, True,
+                               max_q_len=max(b.q_lens), rows=listed)
+    torch.cuda.synchronize()
+    with pytest.raises(RuntimeError, match=match):
+        check_device_errors()
+    sl = slice(b.q_starts[1], b.q_starts[2] + b.q_lens[2])  # rows 1 and 2
+    assert_close(o.float().cpu().numpy()[sl], lse.cpu().numpy()[sl], o_ref[sl], lse_ref[sl], torch.bfloat16)
+
+
 def test_dispatch_mixed_decode_and_prefill_rows():
     """paged_flash_attention sends q_len == 1 rows to the decode kernel and
     q_len > 1 rows to the tcgen05 prefill kernel; together they match the oracle."""
